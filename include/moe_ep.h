@@ -1,0 +1,134 @@
+/*
+ * moe_ep.h — C ABI of the B200 fused MoE expert-parallel layer
+ * (libmoe_ep.so, built from nvshmem_testing_b200/csrc).
+ *
+ * Every entry point is extern "C", takes plain pointers and sizes, and
+ * returns an int status (MOE_EP_OK on success).  Device pointers are CUDA
+ * device addresses; `stream` is a cudaStream_t passed as void*.  No call
+ * synchronises the stream unless stated.
+ *
+ * Which reference interface each entry point replaces (paths are within the
+ * jy1534/nvshmem_testing project):
+ *   moe_route, moe_pack_padded  utils.py:28-69  (bucketize, pad, coalesce)
+ *   moe_symm_*                  alltoall_persistent_gemm.py:161-204
+ *                               (_get_symm_buffers: symmetric receive and
+ *                               signal buffers, rendezvous)
+ *   moe_ep_workspace_layout     alltoall_persistent_gemm.py:187-195
+ *                               (receive [W*transmit, H] + signal [W] shapes)
+ *   moe_ep_run                  alltoall_persistent_gemm.py:207-309 (run:
+ *                               peer copies + flags + fused grouped GEMM) and
+ *                               baseline.py:8-56 (same output contract)
+ */
+#ifndef MOE_EP_H
+#define MOE_EP_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  Device-side errors are also latched in the workspace status
+ * word as (code << 24) | (site << 16) | detail. */
+#define MOE_EP_OK 0
+#define MOE_EP_BAD_ARG 1
+#define MOE_EP_CUDA_ERR 2
+#define MOE_EP_TIMEOUT 3
+#define MOE_EP_CAPACITY 4
+#define MOE_EP_BAD_ROUTE 5
+
+#define MOE_EP_ABI_VERSION 1
+
+int moe_ep_abi_version(void);
+const char* moe_ep_status_string(int code);
+/* Number of SMs of `device`. */
+int moe_ep_num_sms(int device, int* out);
+
+/* ---------------------------------------------------------------- routing
+ * Replaces the per-expert mask loop of utils.py:28-41.
+ *   top_idxs  [T, K] int32 (ids_are_int64 = 0) or int64 (= 1) expert ids
+ *   counts    [E]    tokens per expert; a token counts once per expert even
+ *                    if the id repeats in its row (utils.py:31 `.any(-1)`);
+ *                    ids outside [0, E) match no expert.
+ *   offsets   [E+1]  exclusive scan of counts
+ *   perm      [T*K]  perm[offsets[e] + j] = j-th token (ascending) of expert e
+ *   max_count [1]    max over e of counts[e] (utils.py:45, local max)
+ * E <= 1024.  One CTA; suited to T up to ~10^5 tokens. */
+int moe_route(const void* top_idxs, int ids_are_int64, int64_t T, int K, int E, int32_t* counts, int32_t* offsets,
+              int32_t* perm, int32_t* max_count, void* stream);
+
+/* Replaces utils.py:54-69: out[e*gm + j, :] = tokens[perm[offsets[e] + j], :]
+ * for j < counts[e] and zero rows for counts[e] <= j < gm.  Requires
+ * H * elem_bytes % 16 == 0 and gm >= max(counts). */
+int moe_pack_padded(const void* tokens, int64_t H, int elem_bytes, const int32_t* counts, const int32_t* offsets,
+                    const int32_t* perm, int E, int64_t gm, void* out, void* stream);
+
+/* ---------------------------------------------------------------- symmetric memory
+ * Replaces the torch symmetric-memory allocation + rendezvous of
+ * alltoall_persistent_gemm.py:161-204 with cuMem VMM: the owner allocates
+ * device memory exportable as a POSIX file descriptor; each peer imports the
+ * descriptor (passed over a Unix socket by the host) and maps it. */
+int moe_symm_alloc(int device, size_t bytes, size_t* mapped_bytes, uint64_t* ptr, int* fd, uint64_t* handle);
+int moe_symm_import(int device, int fd, size_t bytes, uint64_t* ptr, uint64_t* handle);
+int moe_symm_free(uint64_t ptr, size_t bytes, uint64_t handle);
+
+/* Byte layout of one rank's symmetric workspace (identical on every rank). */
+typedef struct moe_ep_layout {
+  uint64_t off_cmat;   /* int32 [2][W owner][W src][El]: published recv counts  */
+  uint64_t off_cflag;  /* uint32 [2][W owner]: count arrival epochs            */
+  uint64_t off_dflag;  /* uint32 [2][W src][El][max_chunks]: row-chunk epochs  */
+  uint64_t off_free;   /* uint32 [W peer]: last epoch the peer finished        */
+  uint64_t off_local;  /* uint32 [8]: work counters and the status word        */
+  uint64_t ctrl_bytes; /* bytes [0, ctrl_bytes) must start zeroed              */
+  uint64_t off_data;   /* element [2][cap_rows][H]: compact remote rows        */
+  uint64_t total_bytes;
+} moe_ep_layout;
+
+int moe_ep_workspace_layout(int W, int El, int64_t H, int elem_bytes, int64_t cap_rows, int max_chunks,
+                            moe_ep_layout* out);
+
+/* Zero the control region [0, ctrl_bytes) of a freshly allocated workspace
+ * (counts, flags, epochs, counters).  Every rank must do this, and all ranks
+ * must have done it, before the first moe_ep_run on the workspace. */
+int moe_ep_workspace_reset(uint64_t local_base, const moe_ep_layout* layout, void* stream);
+
+/* ---------------------------------------------------------------- fused layer
+ * Replaces alltoall_persistent_gemm.run (alltoall_persistent_gemm.py:207-309):
+ *   out[le, src*gm + i, :] = tokens_src[(rank*El + le)*gm + i, :] @ weights[le]
+ * for i < recv_counts[src, le]; rows i >= recv_counts[src, le] are written as
+ * zeros.  bf16 in, fp32 accumulate, bf16 out.
+ * Collective: every rank calls with the same W, El, gm, H, N, epoch. */
+typedef struct moe_ep_run_params {
+  int32_t world_size;          /* W                                                  */
+  int32_t rank;                /* this rank                                          */
+  int32_t local_experts;       /* El                                                 */
+  int32_t hidden;              /* H: GEMM K, multiple of 8                           */
+  int32_t out_dim;             /* N: multiple of 8                                   */
+  int32_t elem_bytes;          /* 2 (bf16)                                           */
+  int64_t gm;                  /* padded rows per (rank, expert) slot                */
+  const void* tokens;          /* [W*El*gm, H] this rank's padded send buffer        */
+  const void* weights;         /* [El, H, N] local experts, N contiguous             */
+  const int32_t* recv_counts;  /* [W, El] rows this rank receives per (src, expert)  */
+  void* out;                   /* [El, W*gm, N]                                      */
+  const uint64_t* peer_bases;  /* device array [W]: every rank's workspace, mapped  */
+  uint64_t local_base;         /* this rank's workspace base address                */
+  int64_t cap_rows;            /* remote receive capacity (rows) per parity          */
+  int32_t push_rows;           /* rows per push item and arrival flag                */
+  int32_t max_chunks;          /* flag slots per (src, expert)                       */
+  uint32_t epoch;              /* call counter: 1, 2, 3, ... identical on all ranks  */
+  uint32_t num_ctas;           /* 0 = one CTA per SM                                 */
+  uint64_t timeout_ns;         /* bound on every wait for a peer                     */
+  int32_t* status_host;        /* optional mapped pinned word for device errors      */
+} moe_ep_run_params;
+
+int moe_ep_run(const moe_ep_run_params* params, void* stream);
+
+/* Copy the workspace status word to the host (synchronous). */
+int moe_ep_read_status(uint64_t local_base, const moe_ep_layout* layout, uint32_t* out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOE_EP_H */

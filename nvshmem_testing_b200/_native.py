@@ -1,0 +1,104 @@
+"""ctypes binding of libmoe_ep.so (the C ABI declared in include/moe_ep.h).
+
+The library is built in-tree by ``nvshmem_testing_b200.build``.  There is no
+fallback: if the library is missing or a symbol is absent, importing the
+binding raises, and every device operation of this package raises with it.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libmoe_ep.so"
+
+OK, BAD_ARG, CUDA_ERR, TIMEOUT, CAPACITY, BAD_ROUTE = 0, 1, 2, 3, 4, 5
+STATUS_NAMES = {OK: "ok", BAD_ARG: "bad argument", CUDA_ERR: "CUDA error", TIMEOUT: "timed out waiting for a peer",
+                CAPACITY: "receive capacity exceeded", BAD_ROUTE: "bad routing input"}
+ABI_VERSION = 1
+
+# Every symbol include/moe_ep.h declares.
+EXPORTED = ["moe_ep_abi_version", "moe_ep_status_string", "moe_ep_num_sms", "moe_route", "moe_pack_padded",
+            "moe_symm_alloc", "moe_symm_import", "moe_symm_free", "moe_ep_workspace_layout", "moe_ep_workspace_reset", "moe_ep_run",
+            "moe_ep_read_status"]
+
+
+class MoeEpError(RuntimeError):
+    """A libmoe_ep call or a device-side check failed."""
+
+    def __init__(self, code: int, what: str, detail: str = ""):
+        self.code = code
+        msg = f"{what}: status {code} ({STATUS_NAMES.get(code, 'unknown')})"
+        super().__init__(msg + (f" {detail}" if detail else ""))
+
+
+class Layout(ctypes.Structure):
+    _fields_ = [("off_cmat", ctypes.c_uint64), ("off_cflag", ctypes.c_uint64), ("off_dflag", ctypes.c_uint64),
+                ("off_free", ctypes.c_uint64), ("off_local", ctypes.c_uint64), ("ctrl_bytes", ctypes.c_uint64),
+                ("off_data", ctypes.c_uint64), ("total_bytes", ctypes.c_uint64)]
+
+
+class RunParams(ctypes.Structure):
+    _fields_ = [("world_size", ctypes.c_int32), ("rank", ctypes.c_int32), ("local_experts", ctypes.c_int32),
+                ("hidden", ctypes.c_int32), ("out_dim", ctypes.c_int32), ("elem_bytes", ctypes.c_int32),
+                ("gm", ctypes.c_int64), ("tokens", ctypes.c_void_p), ("weights", ctypes.c_void_p),
+                ("recv_counts", ctypes.c_void_p), ("out", ctypes.c_void_p), ("peer_bases", ctypes.c_void_p),
+                ("local_base", ctypes.c_uint64), ("cap_rows", ctypes.c_int64), ("push_rows", ctypes.c_int32),
+                ("max_chunks", ctypes.c_int32), ("epoch", ctypes.c_uint32), ("num_ctas", ctypes.c_uint32),
+                ("timeout_ns", ctypes.c_uint64), ("status_host", ctypes.c_void_p)]
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load libmoe_ep.so once; raise if it is missing or incomplete."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise MoeEpError(CUDA_ERR, "libmoe_ep.so not built",
+                         f"(expected {LIB_PATH}; run `python -m nvshmem_testing_b200.build`)")
+    L = ctypes.CDLL(os.fspath(LIB_PATH))
+    for name in EXPORTED:
+        if not hasattr(L, name):
+            raise MoeEpError(CUDA_ERR, f"libmoe_ep.so lacks {name}")
+    c_int, c_i64, c_vp, c_u64, c_sz = ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_size_t
+    P = ctypes.POINTER
+    L.moe_ep_abi_version.restype = c_int
+    L.moe_ep_status_string.restype = ctypes.c_char_p
+    L.moe_ep_status_string.argtypes = [c_int]
+    L.moe_ep_num_sms.argtypes = [c_int, P(c_int)]
+    L.moe_route.argtypes = [c_vp, c_int, c_i64, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp]
+    L.moe_pack_padded.argtypes = [c_vp, c_i64, c_int, c_vp, c_vp, c_vp, c_int, c_i64, c_vp, c_vp]
+    L.moe_symm_alloc.argtypes = [c_int, c_sz, P(c_sz), P(c_u64), P(c_int), P(c_u64)]
+    L.moe_symm_import.argtypes = [c_int, c_int, c_sz, P(c_u64), P(c_u64)]
+    L.moe_symm_free.argtypes = [c_u64, c_sz, c_u64]
+    L.moe_ep_workspace_layout.argtypes = [c_int, c_int, c_i64, c_int, c_i64, c_int, P(Layout)]
+    L.moe_ep_workspace_reset.argtypes = [c_u64, P(Layout), c_vp]
+    L.moe_ep_run.argtypes = [P(RunParams), c_vp]
+    L.moe_ep_read_status.argtypes = [c_u64, P(Layout), P(ctypes.c_uint32)]
+    for name in EXPORTED:
+        if name not in ("moe_ep_status_string",):
+            getattr(L, name).restype = c_int
+    if L.moe_ep_abi_version() != ABI_VERSION:
+        raise MoeEpError(CUDA_ERR, "libmoe_ep.so ABI version mismatch")
+    _lib = L
+    return L
+
+
+def check(code: int, what: str) -> None:
+    if code != OK:
+        raise MoeEpError(code, what)
+
+
+def decode_status_word(w: int) -> tuple[int, int, int]:
+    """Split a device status word into (code, site, detail)."""
+    return (w >> 24) & 0xFF, (w >> 16) & 0xFF, w & 0xFFFF
+
+
+def workspace_layout(W: int, El: int, H: int, elem_bytes: int, cap_rows: int, max_chunks: int) -> Layout:
+    L = Layout()
+    check(lib().moe_ep_workspace_layout(W, El, H, elem_bytes, cap_rows, max_chunks, ctypes.byref(L)),
+          "moe_ep_workspace_layout")
+    return L

@@ -1,0 +1,118 @@
+"""Drop-in ``run`` of the reference's fused all-to-all + grouped GEMM path.
+
+Same positional signature, tensor layouts and preconditions as
+alltoall_persistent_gemm.py:207-226 of the reference:
+
+    run(rank, tokens, transmit_size, batch, seq, hidden_dim, num_experts,
+        world_size, shmem=None, general_a2a=False, local_weights=None,
+        recv_counts=None) -> Tensor[El, world_size*gm, out_dim]
+
+with ``tokens`` the padded, expert-major send buffer ``[W*transmit_size, H]``
+(rank d's chunk is rows ``[d*transmit_size, (d+1)*transmit_size)``, itself
+``[El, gm, H]``), ``gm = transmit_size // El``, ``local_weights [El, H, N]``
+and ``recv_counts [W, El]`` int32 (rows received from each source for each
+local expert; all ``gm`` when omitted, alltoall_persistent_gemm.py:286-288).
+Output row ``src*gm + i`` of expert ``le`` is ``recv_tokens @ W[le]`` for
+``i < recv_counts[src, le]`` and exactly zero otherwise
+(alltoall_persistent_gemm.py:257-258, 273-291).
+
+The work runs in one launch of the sm_100a kernel ``moe_ep_run``
+(libmoe_ep.so): counts are exchanged through the symmetric workspace, only
+valid rows cross NVLink, and each GEMM tile starts when its rows have
+landed.  The call is collective over the process group, is stream-ordered on
+the caller's current stream, and does not synchronise the host (the
+reference synchronises twice per call, :237-240).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+import torch.distributed as dist
+
+from . import _native as N
+from .symm import get_workspace
+
+DEFAULT_PUSH_ROWS = int(os.environ.get("MOE_EP_PUSH_ROWS", "32"))
+DEFAULT_TIMEOUT_S = float(os.environ.get("MOE_EP_TIMEOUT_S", "20"))
+
+
+def _group_info(group, world_size: int, rank: int) -> tuple[int, int]:
+    if dist.is_available() and dist.is_initialized():
+        return dist.get_rank(group), dist.get_world_size(group)
+    return rank, world_size
+
+
+def raise_if_device_error(ws) -> None:
+    """Raise if an earlier launch on this workspace latched a device error."""
+    w = ws.host_status()
+    if w:
+        code, site, detail = N.decode_status_word(w)
+        raise N.MoeEpError(code, "moe_ep_run (device)", f"site={site} detail={detail}; the workspace is unusable")
+
+
+def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: int, hidden_dim: int,
+        num_experts: int, world_size: int, shmem=None, general_a2a: bool = False,
+        local_weights: torch.Tensor = None, recv_counts: torch.Tensor = None, *, group=None,
+        timeout_s: float | None = None, push_rows: int | None = None, num_ctas: int = 0,
+        check: bool = False) -> torch.Tensor:
+    """Fused dispatch + grouped GEMM; see the module docstring.
+
+    Keyword-only extensions: ``group`` (process group, default WORLD),
+    ``timeout_s`` (bound on every device wait for a peer), ``push_rows``
+    (rows per NVLink chunk and arrival flag), ``num_ctas`` (0 = one per SM),
+    ``check`` (synchronise and raise on a device error before returning).
+    """
+    if general_a2a:
+        raise NotImplementedError("general/unbalanced a2a not implemented.")
+    assert dist.is_initialized()
+    assert tokens.is_cuda
+    assert tokens.shape[0] == transmit_size * world_size
+    if local_weights is None:
+        raise ValueError("local_weights [El, H, N] is required")
+    me, W = _group_info(group, world_size, rank)
+    if W != world_size or me != rank:
+        raise ValueError(f"rank/world_size ({rank}/{world_size}) disagree with the process group ({me}/{W})")
+    El, H, Nout = local_weights.shape
+    if tokens.dim() != 2 or tokens.shape[1] != H or H != hidden_dim:
+        raise ValueError(f"tokens {tuple(tokens.shape)} / hidden_dim {hidden_dim} do not match weights {tuple(local_weights.shape)}")
+    if transmit_size % El:
+        raise ValueError(f"transmit_size {transmit_size} is not a multiple of the {El} local experts")
+    if tokens.dtype != torch.bfloat16 or local_weights.dtype != torch.bfloat16:
+        raise TypeError("tokens and local_weights must be bfloat16")
+    if local_weights.device != tokens.device:
+        raise ValueError("tokens and local_weights must be on the same device")
+    gm = transmit_size // El
+    dev = tokens.device.index if tokens.device.index is not None else torch.cuda.current_device()
+    tokens = tokens.contiguous()
+    local_weights = local_weights.contiguous()
+    if recv_counts is None:
+        recv_counts = torch.full((W, El), gm, dtype=torch.int32, device=tokens.device)
+    else:
+        if tuple(recv_counts.shape) != (W, El):
+            raise ValueError(f"recv_counts must be [{W}, {El}], got {tuple(recv_counts.shape)}")
+        recv_counts = recv_counts.to(device=tokens.device, dtype=torch.int32).contiguous()
+
+    rows = push_rows or DEFAULT_PUSH_ROWS
+    ws = get_workspace(W, El, H, gm, dev, group, me, rows)
+    raise_if_device_error(ws)
+    out = torch.empty((El, W * gm, Nout), dtype=torch.bfloat16, device=tokens.device)
+
+    p = N.RunParams()
+    p.world_size, p.rank, p.local_experts = W, me, El
+    p.hidden, p.out_dim, p.elem_bytes, p.gm = H, Nout, 2, gm
+    p.tokens, p.weights = tokens.data_ptr(), local_weights.data_ptr()
+    p.recv_counts, p.out = recv_counts.data_ptr(), out.data_ptr()
+    p.peer_bases, p.local_base = ws.peer_bases.data_ptr(), ws.base
+    p.cap_rows, p.push_rows, p.max_chunks = ws.key.cap_rows, ws.push_rows, ws.key.max_chunks
+    p.epoch = ws.next_epoch()
+    p.num_ctas = num_ctas
+    p.timeout_ns = int((timeout_s if timeout_s is not None else DEFAULT_TIMEOUT_S) * 1e9)
+    p.status_host = ws.status_host.data_ptr()
+    stream = torch.cuda.current_stream(tokens.device)
+    N.check(N.lib().moe_ep_run(ctypes.byref(p), ctypes.c_void_p(stream.cuda_stream)), "moe_ep_run")
+    if check:
+        stream.synchronize()
+        raise_if_device_error(ws)
+    return out

@@ -1,0 +1,52 @@
+// Internal declarations shared by the .cu files of the extension.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+
+namespace moe {
+
+// Status codes; identical to the MOE_EP_* values of include/moe_ep.h.
+enum : int {
+  kOk = 0,
+  kBadArg = 1,
+  kCudaErr = 2,
+  kTimeout = 3,
+  kCapacity = 4,
+  kBadRoute = 5,
+};
+
+constexpr int kMaxExperts = 1024;  // routing kernel: experts per call
+
+// ---- routing (route.cu)
+size_t route_smem_bytes(int E);
+int launch_route(const void* ids, int ids_are_int64, int64_t T, int K, int E, int32_t* counts, int32_t* offsets,
+                 int32_t* perm, int32_t* max_count, cudaStream_t stream);
+int launch_pack_padded(const void* tokens, int64_t H, int elem_bytes, const int32_t* counts, const int32_t* offsets,
+                       const int32_t* perm, int E, int64_t gm, void* out, int num_sms, cudaStream_t stream);
+
+// ---- driver entry points (driver.cu), resolved at first use through the runtime
+struct Driver {
+  CUresult (*cuMemGetAllocationGranularity)(size_t*, const CUmemAllocationProp*, CUmemAllocationGranularity_flags);
+  CUresult (*cuMemCreate)(CUmemGenericAllocationHandle*, size_t, const CUmemAllocationProp*, unsigned long long);
+  CUresult (*cuMemAddressReserve)(CUdeviceptr*, size_t, size_t, CUdeviceptr, unsigned long long);
+  CUresult (*cuMemMap)(CUdeviceptr, size_t, size_t, CUmemGenericAllocationHandle, unsigned long long);
+  CUresult (*cuMemSetAccess)(CUdeviceptr, size_t, const CUmemAccessDesc*, size_t);
+  CUresult (*cuMemExportToShareableHandle)(void*, CUmemGenericAllocationHandle, CUmemAllocationHandleType,
+                                           unsigned long long);
+  CUresult (*cuMemImportFromShareableHandle)(CUmemGenericAllocationHandle*, void*, CUmemAllocationHandleType);
+  CUresult (*cuMemUnmap)(CUdeviceptr, size_t);
+  CUresult (*cuMemRelease)(CUmemGenericAllocationHandle);
+  CUresult (*cuMemAddressFree)(CUdeviceptr, size_t);
+  CUresult (*cuTensorMapEncodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                     const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                     CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  bool ok;
+};
+const Driver& driver();
+
+// ---- fused dispatch + grouped GEMM (fused.cu)
+struct RunArgs;  // mirrors moe_ep_run_params (include/moe_ep.h)
+}  // namespace moe

@@ -1,0 +1,223 @@
+// Routing kernels: per-expert counts, expert offsets, the stable token
+// permutation, and the padded expert-major pack.
+//
+// These restate, on the device, the host loop of the reference's router
+// post-processing (utils.py:28-69):
+//   for ex in range(E): mask = (top_idxs == ex).any(-1); bucket = tokens[mask]
+// i.e. a token joins bucket e at most once however often e appears in its
+// top-k row, buckets keep ascending token order, ids outside [0, E) never
+// match any bucket, and every bucket is zero-padded to gm rows and
+// concatenated expert-major.
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "ptx.cuh"
+#include "moe_ep_internal.h"
+
+namespace moe {
+
+constexpr int kRouteThreads = 1024;   // one CTA; one token per thread per chunk
+constexpr int kRouteChunk = 1024;     // tokens per bitmap chunk
+constexpr int kRouteWords = kRouteChunk / 32;
+
+template <typename IdT>
+__device__ __forceinline__ int load_id(const IdT* ids, int64_t i, int E) {
+  const long long v = static_cast<long long>(ids[i]);
+  return (v >= 0 && v < E) ? static_cast<int>(v) : -1;
+}
+
+// True if slot k of row t repeats an earlier slot of the same row.
+template <typename IdT>
+__device__ __forceinline__ bool repeated(const IdT* row, int k, long long v) {
+  for (int j = 0; j < k; ++j)
+    if (static_cast<long long>(row[j]) == v) return true;
+  return false;
+}
+
+// Block-wide exclusive scan of one int per thread (kRouteThreads threads).
+__device__ int block_exclusive_scan(int v, int* warp_sums, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_sums[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int s = warp_sums[lane];
+    int t = s;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int y = __shfl_up_sync(0xffffffffu, t, o);
+      if (lane >= o) t += y;
+    }
+    warp_sums[lane] = t - s;  // exclusive prefix of warp sums
+    if (lane == 31) *total = t;
+  }
+  __syncthreads();
+  const int r = x - v + warp_sums[warp];
+  __syncthreads();
+  return r;
+}
+
+// Single-CTA routing: counts, offsets (exclusive scan), permutation, max.
+// Dynamic shared memory: E * (4 + 4 + 128 + 64) bytes + scan scratch.
+template <typename IdT>
+__global__ void __launch_bounds__(kRouteThreads, 1)
+    route_kernel(const IdT* __restrict__ ids, int64_t T, int K, int E, int32_t* __restrict__ counts,
+                 int32_t* __restrict__ offsets, int32_t* __restrict__ perm, int32_t* __restrict__ max_count) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  int* cnt = reinterpret_cast<int*>(smem_raw);                       // [E]
+  int* cursor = cnt + E;                                             // [E]
+  uint32_t* bits = reinterpret_cast<uint32_t*>(cursor + E);          // [E][32]
+  uint16_t* wpre = reinterpret_cast<uint16_t*>(bits + size_t(E) * kRouteWords);  // [E][32]
+  __shared__ int warp_sums[32];
+  __shared__ int scan_total;
+
+  const int tid = threadIdx.x;
+  for (int e = tid; e < E; e += kRouteThreads) cnt[e] = 0;
+  __syncthreads();
+
+  // Pass 1: counts with per-row de-duplication (the reference's .any(-1)).
+  for (int64_t t = tid; t < T; t += kRouteThreads) {
+    const IdT* row = ids + t * K;
+    for (int k = 0; k < K; ++k) {
+      const int e = load_id(row, k, E);
+      if (e < 0 || repeated(row, k, static_cast<long long>(row[k]))) continue;
+      atomicAdd(&cnt[e], 1);
+    }
+  }
+  __syncthreads();
+
+  // Exclusive scan of counts over experts (E <= kMaxExperts, in slabs of 1024).
+  int carry = 0, mx = 0;
+  for (int base = 0; base < E; base += kRouteThreads) {
+    const int e = base + tid;
+    const int v = e < E ? cnt[e] : 0;
+    mx = max(mx, v);
+    const int ex = block_exclusive_scan(v, warp_sums, &scan_total);
+    if (e < E) {
+      offsets[e] = carry + ex;
+      cursor[e] = carry + ex;
+      counts[e] = v;
+    }
+    carry += scan_total;
+    __syncthreads();
+  }
+  // Block max.
+  for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((tid & 31) == 0) warp_sums[tid >> 5] = mx;
+  __syncthreads();
+  if (tid == 0) {
+    int m = 0;
+    for (int w = 0; w < kRouteThreads / 32; ++w) m = max(m, warp_sums[w]);
+    *max_count = m;
+    offsets[E] = carry;
+  }
+  __syncthreads();
+
+  // Pass 2: stable scatter, one chunk of kRouteChunk tokens at a time.  A
+  // token's rank inside its bucket is the number of earlier tokens in the
+  // chunk holding that expert (popcount of a per-expert bitmap) plus the
+  // bucket cursor carried over from earlier chunks.
+  for (int64_t c0 = 0; c0 < T; c0 += kRouteChunk) {
+    for (int i = tid; i < E * kRouteWords; i += kRouteThreads) bits[i] = 0u;
+    __syncthreads();
+    const int64_t t = c0 + tid;
+    const int w = tid >> 5, b = tid & 31;
+    if (t < T) {
+      const IdT* row = ids + t * K;
+      for (int k = 0; k < K; ++k) {
+        const int e = load_id(row, k, E);
+        if (e >= 0) atomicOr(&bits[size_t(e) * kRouteWords + w], 1u << b);
+      }
+    }
+    __syncthreads();
+    for (int e = tid; e < E; e += kRouteThreads) {
+      int run = 0;
+      for (int j = 0; j < kRouteWords; ++j) {
+        wpre[size_t(e) * kRouteWords + j] = static_cast<uint16_t>(run);
+        run += __popc(bits[size_t(e) * kRouteWords + j]);
+      }
+    }
+    __syncthreads();
+    if (t < T) {
+      const IdT* row = ids + t * K;
+      const uint32_t below = (1u << b) - 1u;
+      for (int k = 0; k < K; ++k) {
+        const int e = load_id(row, k, E);
+        if (e < 0 || repeated(row, k, static_cast<long long>(row[k]))) continue;
+        const size_t s = size_t(e) * kRouteWords + w;
+        const int pos = cursor[e] + wpre[s] + __popc(bits[s] & below);
+        perm[pos] = static_cast<int32_t>(t);
+      }
+    }
+    __syncthreads();
+    for (int e = tid; e < E; e += kRouteThreads) {
+      const size_t s = size_t(e) * kRouteWords + (kRouteWords - 1);
+      cursor[e] += wpre[s] + __popc(bits[s]);
+    }
+    __syncthreads();
+  }
+}
+
+// Padded expert-major pack: out[e*gm + j] = tokens[perm[offsets[e] + j]] for
+// j < counts[e], zero rows for counts[e] <= j < gm.  One warp per output row,
+// 16-byte vectors (row bytes must be a multiple of 16).
+__global__ void pack_padded_kernel(const uint4* __restrict__ tokens, int64_t row_vecs,
+                                   const int32_t* __restrict__ counts, const int32_t* __restrict__ offsets,
+                                   const int32_t* __restrict__ perm, int E, int64_t gm, uint4* __restrict__ out) {
+  const int64_t warps_total = int64_t(gridDim.x) * (blockDim.x >> 5);
+  const int64_t rows = int64_t(E) * gm;
+  const int lane = threadIdx.x & 31;
+  for (int64_t r = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps_total) {
+    const int e = static_cast<int>(r / gm);
+    const int64_t j = r - int64_t(e) * gm;
+    uint4* dst = out + r * row_vecs;
+    if (j < counts[e]) {
+      const uint4* src = tokens + int64_t(perm[offsets[e] + j]) * row_vecs;
+      for (int64_t v = lane; v < row_vecs; v += 32) dst[v] = ld_nc_v4(src + v);
+    } else {
+      const uint4 z = make_uint4(0, 0, 0, 0);
+      for (int64_t v = lane; v < row_vecs; v += 32) dst[v] = z;
+    }
+  }
+}
+
+size_t route_smem_bytes(int E) { return size_t(E) * (4 + 4 + 4 * kRouteWords + 2 * kRouteWords); }
+
+int launch_route(const void* ids, int ids_are_int64, int64_t T, int K, int E, int32_t* counts, int32_t* offsets,
+                 int32_t* perm, int32_t* max_count, cudaStream_t stream) {
+  const size_t smem = route_smem_bytes(E);
+  cudaError_t err;
+  if (ids_are_int64) {
+    err = cudaFuncSetAttribute(route_kernel<long long>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (err != cudaSuccess) return kCudaErr;
+    route_kernel<long long><<<1, kRouteThreads, smem, stream>>>(static_cast<const long long*>(ids), T, K, E, counts,
+                                                              offsets, perm, max_count);
+  } else {
+    err = cudaFuncSetAttribute(route_kernel<int32_t>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (err != cudaSuccess) return kCudaErr;
+    route_kernel<int32_t><<<1, kRouteThreads, smem, stream>>>(static_cast<const int32_t*>(ids), T, K, E, counts,
+                                                            offsets, perm, max_count);
+  }
+  return cudaGetLastError() == cudaSuccess ? kOk : kCudaErr;
+}
+
+int launch_pack_padded(const void* tokens, int64_t H, int elem_bytes, const int32_t* counts, const int32_t* offsets,
+                       const int32_t* perm, int E, int64_t gm, void* out, int num_sms, cudaStream_t stream) {
+  const int64_t row_vecs = H * elem_bytes / 16;
+  const int64_t rows = int64_t(E) * gm;
+  if (rows == 0) return kOk;
+  const int threads = 256;
+  int64_t blocks = (rows + (threads / 32) - 1) / (threads / 32);
+  const int64_t cap = int64_t(num_sms) * 8;
+  if (blocks > cap) blocks = cap;
+  pack_padded_kernel<<<int(blocks), threads, 0, stream>>>(static_cast<const uint4*>(tokens), row_vecs, counts,
+                                                          offsets, perm, E, gm, static_cast<uint4*>(out));
+  return cudaGetLastError() == cudaSuccess ? kOk : kCudaErr;
+}
+
+}  // namespace moe

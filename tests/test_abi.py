@@ -1,0 +1,69 @@
+"""The C-ABI library loads on a host without a GPU, exports every symbol its
+header declares, and validates arguments before touching the device."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from nvshmem_testing_b200 import _native as N
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "moe_ep.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^(?:int|const char\*)\s+(moe_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    names = declared_functions()
+    assert len(names) >= 10
+    lib = N.lib()
+    for n in names:
+        assert hasattr(lib, n), n
+    assert set(names) == set(N.EXPORTED)
+
+
+def test_abi_version_and_status_strings():
+    lib = N.lib()
+    assert lib.moe_ep_abi_version() == N.ABI_VERSION
+    assert lib.moe_ep_status_string(N.TIMEOUT) == b"timed out waiting for a peer"
+    assert lib.moe_ep_status_string(99) == b"unknown status"
+
+
+def test_workspace_layout_is_host_only_and_aligned():
+    L = N.workspace_layout(8, 32, 7168, 2, 7 * 32 * 256, 8)
+    assert L.ctrl_bytes <= L.off_data and L.off_data % 4096 == 0
+    assert L.total_bytes >= L.off_data + 2 * 7 * 32 * 256 * 7168 * 2
+    offs = [L.off_cmat, L.off_cflag, L.off_dflag, L.off_free, L.off_local]
+    assert offs == sorted(offs) and all(o % 256 == 0 for o in offs)
+    # count matrix: two parities of [W][W][El] int32
+    assert L.off_cflag - L.off_cmat >= 2 * 8 * 8 * 32 * 4
+    assert L.off_free - L.off_dflag >= 2 * 8 * 32 * 8 * 4
+
+
+def test_bad_arguments_are_rejected_before_any_device_call():
+    lib = N.lib()
+    assert lib.moe_route(None, 0, 10, 1, 4, None, None, None, None, None) == N.BAD_ARG
+    assert lib.moe_route(None, 0, 0, 1, 5000, None, None, None, None, None) == N.BAD_ARG
+    assert lib.moe_pack_padded(None, 7, 2, None, None, None, 4, 1, None, None) == N.BAD_ARG
+    assert lib.moe_ep_run(None, None) == N.BAD_ARG
+    p = N.RunParams()
+    p.world_size, p.rank, p.local_experts, p.hidden, p.out_dim, p.elem_bytes = 2, 2, 1, 64, 64, 2
+    assert lib.moe_ep_run(ctypes.byref(p), None) == N.BAD_ARG  # rank out of range
+    p.rank, p.hidden = 0, 60  # H not a multiple of 8
+    assert lib.moe_ep_run(ctypes.byref(p), None) == N.BAD_ARG
+    bad = N.Layout()
+    assert lib.moe_ep_workspace_layout(0, 1, 1, 2, 0, 1, ctypes.byref(bad)) == N.BAD_ARG
+
+
+def test_status_word_decoding():
+    assert N.decode_status_word((3 << 24) | (4 << 16) | 7) == (3, 4, 7)
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    monkeypatch.setattr(N, "_lib", None)
+    monkeypatch.setattr(N, "LIB_PATH", tmp_path / "absent.so")
+    with pytest.raises(N.MoeEpError):
+        N.lib()

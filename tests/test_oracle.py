@@ -1,0 +1,126 @@
+"""The oracle against the reference's own outputs (golden fixtures) and its
+own edge cases.  CPU only."""
+import hashlib
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from nvshmem_testing_b200 import workloads
+from conftest import GOLDEN
+
+
+def _routing_cases():
+    g = np.load(GOLDEN / "routing_golden.npz")
+    return g, int(g["num_cases"][0])
+
+
+def test_routing_matches_reference_gen_tensor():
+    """utils.gen_tensor of the reference, bit for bit: lengths, chunk_size and
+    the coalesced tensor (SHA-256), with the reference's local max as gm."""
+    g, n = _routing_cases()
+    assert n >= 10
+    for ci in range(n):
+        p = f"c{ci}_"
+        b, s, h, e, k, w, r = (int(x) for x in g[p + "shape"])
+        tokens = g[p + "tokens"]
+        ids = g[p + "top_idxs"].astype(np.int64)
+        assert tokens.shape == (b * s, h) and ids.shape == (b * s, k)
+        coalesced, chunk, lengths = oracle.gen_tensor_restated(tokens, ids, e, w)
+        assert lengths == g[p + "lengths"].tolist(), ci
+        assert chunk == int(g[p + "chunk"][0]), ci
+        assert coalesced.shape[0] == int(g[p + "coalesced_rows"][0]), ci
+        digest = hashlib.sha256(np.ascontiguousarray(coalesced).tobytes()).digest()
+        assert digest == g[p + "coalesced_sha256"].tobytes(), ci
+        if p + "coalesced" in g:
+            assert np.array_equal(coalesced, g[p + "coalesced"])
+
+
+def test_layer_matches_reference_baseline_run():
+    """baseline.run of the reference under gloo (2 CPU ranks, fp32)."""
+    g = np.load(GOLDEN / "layer_golden.npz")
+    W = int(g["world"][0])
+    gm = int(g["gm"][0])
+    wl = workloads.get("cpu_gloo")
+    El = wl.E // W
+    send, wts = [], []
+    for r in range(W):
+        tok = workloads.tokens(wl, r).numpy()
+        wt = workloads.weights(wl, r, W).numpy()
+        assert hashlib.sha256(tok.tobytes()).digest() == g[f"r{r}_tokens_sha256"].tobytes()
+        assert hashlib.sha256(wt.tobytes()).digest() == g[f"r{r}_weights_sha256"].tobytes()
+        ids = workloads.top_idxs(wl, r).numpy()
+        assert np.array_equal(ids, g[f"r{r}_top_idxs"].astype(np.int64))
+        counts, offsets, perm = oracle.bucketize(ids, wl.E)
+        assert np.array_equal(counts, g[f"r{r}_counts"])
+        send.append(oracle.pad_coalesce(tok, counts, offsets, perm, gm))
+        wts.append(wt)
+    outs = oracle.ep_layer(send, gm * El, wts)
+    for r in range(W):
+        ref = g[f"r{r}_out"]
+        assert outs[r].shape == ref.shape
+        np.testing.assert_allclose(outs[r], ref, rtol=1e-5, atol=1e-5)
+
+
+def test_bucketize_dedup_and_out_of_range():
+    ids = np.array([[1, 1], [0, 3], [7, -1], [3, 0], [2, 2]])
+    counts, offsets, perm = oracle.bucketize(ids, 4)
+    assert counts.tolist() == [2, 1, 1, 2]
+    assert offsets.tolist() == [0, 2, 3, 4, 6]
+    assert perm.tolist() == [1, 3, 0, 4, 1, 3]
+
+
+def test_bucketize_empty_and_ragged():
+    counts, offsets, perm = oracle.bucketize(np.zeros((0, 2), np.int64), 3)
+    assert counts.tolist() == [0, 0, 0] and perm.size == 0
+    assert oracle.local_max(counts) == 1
+    tok = np.arange(10, dtype=np.uint16).reshape(5, 2)
+    ids = np.array([[0], [0], [2], [0], [2]])
+    c, o, p = oracle.bucketize(ids, 3)
+    out = oracle.pad_coalesce(tok, c, o, p, 3)
+    assert out.shape == (9, 2)
+    assert out[:3].tolist() == [[0, 1], [2, 3], [6, 7]]
+    assert not out[3:6].any()
+    assert out[6:8].tolist() == [[4, 5], [8, 9]] and not out[8].any()
+
+
+def test_pad_rejects_small_gm():
+    ids = np.array([[0], [0]])
+    c, o, p = oracle.bucketize(ids, 1)
+    with pytest.raises(ValueError):
+        oracle.pad_coalesce(np.zeros((2, 4), np.uint16), c, o, p, 1)
+
+
+def test_recv_counts_matrix():
+    a = [np.array([1, 2, 3, 4]), np.array([5, 6, 7, 8])]
+    assert oracle.recv_counts_matrix(a, 0, 2).tolist() == [[1, 2], [5, 6]]
+    assert oracle.recv_counts_matrix(a, 1, 2).tolist() == [[3, 4], [7, 8]]
+
+
+def test_bf16_round_trip():
+    x = np.array([1.0, -2.5, 3.140625, 1e-3, 65504.0], np.float32)
+    bits = oracle.f32_to_bf16_bits(x)
+    t = torch.from_numpy(x).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    assert np.array_equal(bits, t)
+    back = oracle.bf16_bits_to_f32(bits)
+    assert np.array_equal(back, torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).float().numpy())
+
+
+@pytest.mark.parametrize("name", ["mixtral", "deepseek_v3", "skewed_zipf", "decode", "cpu_gloo"])
+def test_workload_routing_properties(name):
+    wl = workloads.get(name, T=min(workloads.get(name).T, 512))
+    ids = workloads.top_idxs(wl, 0)
+    assert ids.shape == (wl.T, wl.K)
+    assert int(ids.min()) >= 0 and int(ids.max()) < wl.E
+    if wl.K > 1:  # distinct experts per token
+        s = torch.sort(ids, dim=1).values
+        assert bool((s[:, 1:] != s[:, :-1]).all())
+
+
+def test_zipf_is_skewed_and_shared_across_ranks():
+    wl = workloads.get("skewed_zipf", T=2048)
+    c0 = np.bincount(workloads.top_idxs(wl, 0).flatten().numpy(), minlength=wl.E)
+    c1 = np.bincount(workloads.top_idxs(wl, 1).flatten().numpy(), minlength=wl.E)
+    assert c0.max() > 4 * np.median(c0)
+    assert np.argmax(c0) == np.argmax(c1)  # same popularity order on every rank
