@@ -54,7 +54,7 @@ int moe_ep_num_sms(int device, int* out);
  *   offsets   [E+1]  exclusive scan of counts
  *   perm      [T*K]  perm[offsets[e] + j] = j-th token (ascending) of expert e
  *   max_count [1]    max over e of counts[e] (utils.py:45, local max)
- * E <= 1024.  One CTA; suited to T up to ~10^5 tokens. */
+ * E <= 1024, K <= 32.  One CTA; suited to T up to ~10^5 tokens. */
 int moe_route(const void* top_idxs, int ids_are_int64, int64_t T, int K, int E, int32_t* counts, int32_t* offsets,
               int32_t* perm, int32_t* max_count, void* stream);
 

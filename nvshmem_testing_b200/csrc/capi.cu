@@ -40,7 +40,7 @@ int moe_ep_num_sms(int device, int* out) {
 
 int moe_route(const void* top_idxs, int ids_are_int64, int64_t T, int K, int E, int32_t* counts, int32_t* offsets,
               int32_t* perm, int32_t* max_count, void* stream) {
-  if (T < 0 || K < 1 || E < 1 || E > kMaxExperts || (T > 0 && !top_idxs) || !counts || !offsets || !max_count ||
+  if (T < 0 || K < 1 || K > kMaxRouteK || E < 1 || E > kMaxExperts || (T > 0 && !top_idxs) || !counts || !offsets || !max_count ||
       (T > 0 && !perm))
     return kBadArg;
   if (T * int64_t(K) >= (int64_t(1) << 31)) return kBadArg;

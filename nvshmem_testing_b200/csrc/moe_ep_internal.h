@@ -19,6 +19,7 @@ enum : int {
 };
 
 constexpr int kMaxExperts = 1024;  // routing kernel: experts per call
+constexpr int kMaxRouteK = 32;     // routing kernel: ids per token (top-k width)
 
 // ---- routing (route.cu)
 size_t route_smem_bytes(int E);

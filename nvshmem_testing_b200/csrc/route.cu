@@ -20,18 +20,11 @@ constexpr int kRouteThreads = 1024;   // one CTA; one token per thread per chunk
 constexpr int kRouteChunk = 1024;     // tokens per bitmap chunk
 constexpr int kRouteWords = kRouteChunk / 32;
 
+
 template <typename IdT>
 __device__ __forceinline__ int load_id(const IdT* ids, int64_t i, int E) {
   const long long v = static_cast<long long>(ids[i]);
   return (v >= 0 && v < E) ? static_cast<int>(v) : -1;
-}
-
-// True if slot k of row t repeats an earlier slot of the same row.
-template <typename IdT>
-__device__ __forceinline__ bool repeated(const IdT* row, int k, long long v) {
-  for (int j = 0; j < k; ++j)
-    if (static_cast<long long>(row[j]) == v) return true;
-  return false;
 }
 
 // Block-wide exclusive scan of one int per thread (kRouteThreads threads).
@@ -63,7 +56,9 @@ __device__ int block_exclusive_scan(int v, int* warp_sums, int* total) {
 }
 
 // Single-CTA routing: counts, offsets (exclusive scan), permutation, max.
-// Dynamic shared memory: E * (4 + 4 + 128 + 64) bytes + scan scratch.
+// Dynamic shared memory: E * (4 + 4 + 128 + 64) bytes + scan scratch.  The
+// chunk bitmap is word-major (bits[w][e]) so that threads walking experts
+// touch consecutive banks.
 template <typename IdT>
 __global__ void __launch_bounds__(kRouteThreads, 1)
     route_kernel(const IdT* __restrict__ ids, int64_t T, int K, int E, int32_t* __restrict__ counts,
@@ -71,8 +66,8 @@ __global__ void __launch_bounds__(kRouteThreads, 1)
   extern __shared__ __align__(16) unsigned char smem_raw[];
   int* cnt = reinterpret_cast<int*>(smem_raw);                       // [E]
   int* cursor = cnt + E;                                             // [E]
-  uint32_t* bits = reinterpret_cast<uint32_t*>(cursor + E);          // [E][32]
-  uint16_t* wpre = reinterpret_cast<uint16_t*>(bits + size_t(E) * kRouteWords);  // [E][32]
+  uint32_t* bits = reinterpret_cast<uint32_t*>(cursor + E);          // [32][E]
+  uint16_t* wpre = reinterpret_cast<uint16_t*>(bits + size_t(E) * kRouteWords);  // [32][E]
   __shared__ int warp_sums[32];
   __shared__ int scan_total;
 
@@ -81,12 +76,17 @@ __global__ void __launch_bounds__(kRouteThreads, 1)
   __syncthreads();
 
   // Pass 1: counts with per-row de-duplication (the reference's .any(-1)).
+  // A row's ids are read once; a slot whose id repeats an earlier slot of
+  // the same row is skipped.
   for (int64_t t = tid; t < T; t += kRouteThreads) {
     const IdT* row = ids + t * K;
+    int seen[kMaxRouteK];
     for (int k = 0; k < K; ++k) {
       const int e = load_id(row, k, E);
-      if (e < 0 || repeated(row, k, static_cast<long long>(row[k]))) continue;
-      atomicAdd(&cnt[e], 1);
+      bool dup = false;
+      for (int j = 0; j < k; ++j) dup |= (seen[j] == e);
+      seen[k] = e;
+      if (e >= 0 && !dup) atomicAdd(&cnt[e], 1);
     }
   }
   __syncthreads();
@@ -127,36 +127,39 @@ __global__ void __launch_bounds__(kRouteThreads, 1)
     __syncthreads();
     const int64_t t = c0 + tid;
     const int w = tid >> 5, b = tid & 31;
+    int seen[kMaxRouteK];
     if (t < T) {
       const IdT* row = ids + t * K;
       for (int k = 0; k < K; ++k) {
         const int e = load_id(row, k, E);
-        if (e >= 0) atomicOr(&bits[size_t(e) * kRouteWords + w], 1u << b);
+        seen[k] = e;
+        if (e >= 0) atomicOr(&bits[size_t(w) * E + e], 1u << b);
       }
     }
     __syncthreads();
     for (int e = tid; e < E; e += kRouteThreads) {
       int run = 0;
       for (int j = 0; j < kRouteWords; ++j) {
-        wpre[size_t(e) * kRouteWords + j] = static_cast<uint16_t>(run);
-        run += __popc(bits[size_t(e) * kRouteWords + j]);
+        wpre[size_t(j) * E + e] = static_cast<uint16_t>(run);
+        run += __popc(bits[size_t(j) * E + e]);
       }
     }
     __syncthreads();
     if (t < T) {
-      const IdT* row = ids + t * K;
       const uint32_t below = (1u << b) - 1u;
       for (int k = 0; k < K; ++k) {
-        const int e = load_id(row, k, E);
-        if (e < 0 || repeated(row, k, static_cast<long long>(row[k]))) continue;
-        const size_t s = size_t(e) * kRouteWords + w;
+        const int e = seen[k];
+        bool dup = false;
+        for (int j = 0; j < k; ++j) dup |= (seen[j] == e);
+        if (e < 0 || dup) continue;
+        const size_t s = size_t(w) * E + e;
         const int pos = cursor[e] + wpre[s] + __popc(bits[s] & below);
         perm[pos] = static_cast<int32_t>(t);
       }
     }
     __syncthreads();
     for (int e = tid; e < E; e += kRouteThreads) {
-      const size_t s = size_t(e) * kRouteWords + (kRouteWords - 1);
+      const size_t s = size_t(kRouteWords - 1) * E + e;
       cursor[e] += wpre[s] + __popc(bits[s]);
     }
     __syncthreads();
