@@ -383,10 +383,22 @@ def main(argv=None) -> int:
 
     peaks, peaks_src = load_peaks()
     peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
-    achieved = flops_rank / (ms_max * 1e-3) / 1e12
+    hbm_peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    # Algorithmic HBM bytes of one launch on this rank: expert weights once,
+    # every valid row once, the whole padded output, and the remote rows read
+    # for sending plus written by peers.
+    hbm_bytes = (El * wl.H * wl.N * 2 + rows_in * wl.H * 2 + El * world * gm * wl.N * 2
+                 + (remote_in + remote_out) * wl.H * 2)
     t_gemm_us = flops_rank / (peak * 1e12) * 1e6
+    t_hbm_us = hbm_bytes / (hbm_peak * 1e9) * 1e6
     t_link_us = nvlink_bytes / (NVLINK_GBS * 1e9) * 1e6
-    roof_us = max_over_ranks(max(t_gemm_us, t_link_us))
+    roof_us = max_over_ranks(max(t_gemm_us, t_hbm_us, t_link_us))
+    if t_hbm_us > t_gemm_us:
+        bound, achieved, peak_v, unit = "hbm", hbm_bytes / (ms_max * 1e-3) / 1e9, hbm_peak, "GB/s"
+        peak_note = f"{peaks_src} hbm_gbs"
+    else:
+        bound, achieved, peak_v, unit = "tensor", flops_rank / (ms_max * 1e-3) / 1e12, peak, "TFLOP/s"
+        peak_note = f"{peaks_src} bf16_tflops (burst)"
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_max, "us_per_layer": ms_max * 1e3, "higher_is_better": True,
@@ -395,12 +407,13 @@ def main(argv=None) -> int:
                    "local_experts": El, "top_k": wl.K, "out_dim": wl.N, "routing": wl.routing, "gm": gm,
                    "parallelism": f"ep{world}", "l2": "inputs larger than L2 (weights and tokens > 126 MB)"},
         "parity_vs_nccl_allclose": ok,
-        "roofline": {"bound": "tensor" if t_gemm_us >= t_link_us else "nvlink", "achieved": achieved,
-                     "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                     "peak_source": f"{peaks_src} bf16_tflops (burst)",
-                     "layer_frac": roof_us / (ms_max * 1e3),
-                     "layer_roofline_us": roof_us, "nvlink_bytes_rank0": nvlink_bytes,
-                     "traffic": load_traffic(wl.name, world)},
+        "roofline": {"bound": bound, "achieved": achieved, "peak": peak_v, "unit": unit,
+                     "frac": achieved / peak_v, "peak_source": peak_note,
+                     "traffic": load_traffic(wl.name, world), "algorithmic_hbm_bytes": hbm_bytes,
+                     "tensor_tflops": flops_rank / (ms_max * 1e-3) / 1e12,
+                     "bounds_us": {"tensor": t_gemm_us, "hbm": t_hbm_us, "nvlink": t_link_us},
+                     "layer_roofline_us": roof_us, "layer_frac": roof_us / (ms_max * 1e3),
+                     "nvlink_bytes_rank": nvlink_bytes},
         "cpu_baseline": None,
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "us_per_layer": e2e_ms * 1e3,

@@ -120,7 +120,31 @@ typedef struct moe_ep_run_params {
   uint32_t num_ctas;           /* 0 = one CTA per SM                                 */
   uint64_t timeout_ns;         /* bound on every wait for a peer                     */
   int32_t* status_host;        /* optional mapped pinned word for device errors      */
+  uint64_t* trace;             /* optional device timeline, MOE_EP_TRACE_WORDS per  */
+                               /* CTA (NULL = off); see MOE_EP_TRACE_* below         */
 } moe_ep_run_params;
+
+/* Device timeline (globaltimer ns, or counts), one record per CTA. */
+#define MOE_EP_TRACE_WORDS 24
+#define MOE_EP_TRACE_START 0          /* kernel entry                                */
+#define MOE_EP_TRACE_COUNTS 1         /* all count blocks arrived                    */
+#define MOE_EP_TRACE_SCHED 2          /* schedule built                              */
+#define MOE_EP_TRACE_PRODUCER_END 3   /* TMA producer finished its tiles             */
+#define MOE_EP_TRACE_MMA_END 4        /* MMA issuer finished (leader CTAs)           */
+#define MOE_EP_TRACE_EPI_END 5        /* epilogue finished                           */
+#define MOE_EP_TRACE_PUSH_END 6       /* this CTA's last NVLink push item done       */
+#define MOE_EP_TRACE_ZERO_END 7       /* padded-row zeroing done                     */
+#define MOE_EP_TRACE_END 8            /* teardown done                               */
+#define MOE_EP_TRACE_TILES 9          /* tiles processed (count)                     */
+#define MOE_EP_TRACE_FLAG_WAIT 10     /* ns the producer spent waiting for rows      */
+#define MOE_EP_TRACE_FULL_WAIT 11     /* ns the MMA issuer spent waiting for stages  */
+#define MOE_EP_TRACE_PUSH_ITEMS 12    /* push items done (count)                     */
+#define MOE_EP_TRACE_PUSH_BYTES 13    /* bytes pushed over NVLink                    */
+#define MOE_EP_TRACE_EMPTY_WAIT 14    /* ns the producer spent waiting for free stages */
+#define MOE_EP_TRACE_EPI_WAIT 15      /* ns the epilogue spent waiting for accumulators */
+#define MOE_EP_TRACE_ACC_WAIT 16      /* ns the MMA issuer waited for a free accumulator */
+#define MOE_EP_TRACE_MMA_ISSUE 17     /* ns the MMA issuer spent issuing (not waiting) */
+#define MOE_EP_TRACE_KBLOCKS 18       /* k-blocks issued by the MMA issuer (count)    */
 
 int moe_ep_run(const moe_ep_run_params* params, void* stream);
 

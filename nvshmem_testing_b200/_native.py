@@ -45,7 +45,13 @@ class RunParams(ctypes.Structure):
                 ("recv_counts", ctypes.c_void_p), ("out", ctypes.c_void_p), ("peer_bases", ctypes.c_void_p),
                 ("local_base", ctypes.c_uint64), ("cap_rows", ctypes.c_int64), ("push_rows", ctypes.c_int32),
                 ("max_chunks", ctypes.c_int32), ("epoch", ctypes.c_uint32), ("num_ctas", ctypes.c_uint32),
-                ("timeout_ns", ctypes.c_uint64), ("status_host", ctypes.c_void_p)]
+                ("timeout_ns", ctypes.c_uint64), ("status_host", ctypes.c_void_p), ("trace", ctypes.c_void_p)]
+
+
+TRACE_WORDS = 24
+TRACE_FIELDS = ["start", "counts", "sched", "producer_end", "mma_end", "epi_end", "push_end", "zero_end", "end",
+                "tiles", "flag_wait_ns", "full_wait_ns", "push_items", "push_bytes", "empty_wait_ns",
+                "epi_wait_ns", "acc_wait_ns", "mma_issue_ns", "kblocks"]
 
 
 _lib = None

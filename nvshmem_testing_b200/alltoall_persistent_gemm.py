@@ -56,13 +56,15 @@ def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: in
         num_experts: int, world_size: int, shmem=None, general_a2a: bool = False,
         local_weights: torch.Tensor = None, recv_counts: torch.Tensor = None, *, group=None,
         timeout_s: float | None = None, push_rows: int | None = None, num_ctas: int = 0,
-        check: bool = False) -> torch.Tensor:
+        check: bool = False, trace: torch.Tensor | None = None) -> torch.Tensor:
     """Fused dispatch + grouped GEMM; see the module docstring.
 
     Keyword-only extensions: ``group`` (process group, default WORLD),
     ``timeout_s`` (bound on every device wait for a peer), ``push_rows``
     (rows per NVLink chunk and arrival flag), ``num_ctas`` (0 = one per SM),
-    ``check`` (synchronise and raise on a device error before returning).
+    ``check`` (synchronise and raise on a device error before returning),
+    ``trace`` (int64 device tensor of at least ``num_sms * 24`` words that
+    receives the per-CTA device timeline, ``_native.TRACE_FIELDS``).
     """
     if general_a2a:
         raise NotImplementedError("general/unbalanced a2a not implemented.")
@@ -110,6 +112,10 @@ def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: in
     p.num_ctas = num_ctas
     p.timeout_ns = int((timeout_s if timeout_s is not None else DEFAULT_TIMEOUT_S) * 1e9)
     p.status_host = ws.status_host.data_ptr()
+    if trace is not None:
+        if trace.dtype != torch.int64 or not trace.is_cuda:
+            raise TypeError("trace must be an int64 CUDA tensor")
+        p.trace = trace.data_ptr()
     stream = torch.cuda.current_stream(tokens.device)
     N.check(N.lib().moe_ep_run(ctypes.byref(p), ctypes.c_void_p(stream.cuda_stream)), "moe_ep_run")
     if check:

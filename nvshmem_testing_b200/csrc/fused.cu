@@ -1,6 +1,7 @@
 // Fused expert-parallel layer for sm_100a: count exchange, NVLink dispatch
-// with per-chunk arrival flags, and a persistent tcgen05/TMEM grouped GEMM
-// whose tiles start as soon as the rows they read have landed.
+// with per-chunk arrival flags, and a persistent grouped GEMM on CTA pairs
+// (tcgen05 cta_group::2, TMEM accumulators, TMA) whose tiles start as soon as
+// the rows they read have landed.
 //
 // Reference behaviour (paths within jy1534/nvshmem_testing):
 //   alltoall_persistent_gemm.py:207-309  run(): peer copies of each rank's
@@ -10,14 +11,27 @@
 //   baseline.py:18-50                    same output contract through NCCL
 //       all_to_all_single + view/permute/flatten + bmm; padded rows are zero.
 //
-// B200 design (one CTA per SM, 320 threads):
-//   warp 0      TMA producer: waits for the arrival flags of a tile's rows,
-//               then streams A (token rows, K-major) and B (expert weights,
-//               N-major) k-blocks into a 4-stage shared-memory ring.
-//   warp 1      MMA issuer: one thread issues tcgen05.mma (M=128, N=256,
-//               K=16, bf16 -> f32) into one of two TMEM accumulators.
-//   warps 2-5   epilogue: tcgen05.ld of the accumulator, bf16 convert, store
-//               of the valid rows to out[le, src*gm + m, :].
+// B200 design.  The GEMM is computed transposed, D^T[features, rows] =
+// W^T[features, K] . X^T[K, rows]: expert weights are the MMA A operand
+// (N-contiguous in memory, so "MN-major"), token rows the B operand
+// (K-major), and a tile's row count becomes the MMA N, which can be any
+// multiple of 16 up to 256 — experts with ~130 rows waste at most 15 rows,
+// not a whole 128-row M tile.  Two CTAs of a cluster form a pair: one
+// tcgen05.mma.cta_group::2 (M = 256 features, N = rows, K = 16) reads each
+// CTA's 128 features of A and half of the rows of B from that CTA's shared
+// memory and accumulates into each CTA's TMEM, so each CTA stages only 32 KB
+// per 64-wide k-block (a 6-stage ring).
+//
+// Warp roles (both CTAs of a pair, 320 threads):
+//   warp 0      TMA producer.  The leader CTA waits for the arrival flags of
+//               the tile's rows and forwards a go/abort verdict to the peer;
+//               both then stream their halves; pair loads complete on the
+//               leader's full barrier.
+//   warp 1      MMA issuer (leader only): one thread issues the pair MMAs and
+//               commits to both CTAs' barriers.
+//   warps 2-5   epilogue: tcgen05.ld of this CTA's 128 features, bf16,
+//               transposed through shared memory, 16-byte stores of the valid
+//               rows to out[le, src*gm + m, :].
 //   warps 6-9   dispatch: copy this rank's valid rows for every peer straight
 //               into the peer's receive buffer over NVLink (16-byte vectors),
 //               then release a per-(src, expert, chunk) flag with the call's
@@ -25,15 +39,16 @@
 // Rows this rank sends to itself are never copied: local tiles read them in
 // place from the padded send buffer.  Remote rows land in a compact,
 // expert-major receive buffer (per expert, sources in the order rank+1,
-// rank+2, ...), so one 128-row tile can span several sources.
-// Receive buffers, counts and flags are double-buffered by epoch parity; a
-// peer reuses parity p only after this rank has published that it finished
-// the call that last used it (the "free" epochs), so no per-call barrier or
-// flag reset exists.  Every wait is bounded by timeout_ns; on expiry the
-// kernel latches MOE_EP_TIMEOUT, drains its in-flight copies and MMAs, frees
-// TMEM and returns.
+// rank+2, ...), so a tile can span several sources.  Receive buffers, counts
+// and flags are double-buffered by epoch parity; a peer reuses parity p only
+// after this rank has published that it finished the call that last used it
+// ("free" epochs), so no per-call barrier or flag reset exists.  Every wait is
+// bounded by timeout_ns; on expiry the kernel latches MOE_EP_TIMEOUT, drains
+// its in-flight copies and MMAs, frees TMEM and returns.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
+
+#include <algorithm>
 
 #include "moe_ep.h"
 #include "moe_ep_internal.h"
@@ -41,23 +56,28 @@
 
 namespace moe {
 
-constexpr int BM = 128, BN = 256, BK = 64;
-constexpr int kStages = 4;
+constexpr int BK = 64;                          // k-block (bf16 elements, one 128-byte swizzle row)
+constexpr int kStages = 6;
+constexpr int kFeatPair = 256;                  // output features per pair tile (MMA M)
+constexpr int kFeatCta = 128;                   // features per CTA (TMEM lanes)
+constexpr int kMaxTileRows = 256;               // rows per tile (MMA N)
 constexpr int kEpiWarps = 4;
 constexpr int kPushWarps = 4;
 constexpr int kWarpProducer = 0, kWarpMma = 1, kWarpEpi0 = 2, kWarpPush0 = 2 + kEpiWarps;
 constexpr int kThreads = (2 + kEpiWarps + kPushWarps) * 32;
 constexpr int kPushThreads = kPushWarps * 32;
-constexpr uint32_t kABytes = BM * BK * 2;       // 16 KB
-constexpr uint32_t kBBoxBytes = BK * 64 * 2;    // 8 KB: 64 K-rows x 64 N (128 B)
-constexpr uint32_t kBBytes = BK * BN * 2;       // 32 KB
-constexpr uint32_t kStageBytes = kABytes + kBBytes;
+constexpr uint32_t kABox = 64 * BK * 2;                       // 8 KB: 64 features x 64 K
+constexpr uint32_t kABytes = kFeatCta * BK * 2;               // 16 KB
+constexpr uint32_t kBBytesMax = (kMaxTileRows / 2) * BK * 2;  // 16 KB: 128 rows x 64 K
+constexpr uint32_t kStageBytes = kABytes + kBBytesMax;        // 32 KB
 constexpr int kMaxCells = 512;                  // W * El
 constexpr int kMaxLocalExperts = 256;
-constexpr uint32_t kAccCols = BN;
+constexpr uint32_t kAccCols = kMaxTileRows;
 constexpr uint32_t kTmemCols = 2 * kAccCols;
-constexpr uint32_t kIdesc = make_idesc(/*bf16*/ 1, BM, BN, /*B N-major*/ 1);
+constexpr int kGoSlots = 8;                     // > kStages: the leader runs at most kStages k-blocks ahead
+constexpr int kRowMaps = 5;                     // B boxes of 8, 16, 32, 64, 128 rows
 constexpr int kNamedBarPush = 1;
+constexpr uint32_t kEpiStageBytes = kEpiWarps * 32 * 32 * 2;  // 32 rows x 32 features bf16 per warp
 
 // Where an error was detected (status word "site" byte).
 enum Site : int {
@@ -73,6 +93,7 @@ struct Params {
   int W, me, El, H, N;
   int64_t gm;
   const __nv_bfloat16* tokens;
+  const __nv_bfloat16* weights;
   const int32_t* recv_counts;
   __nv_bfloat16* out;
   const uint64_t* peers;
@@ -83,6 +104,18 @@ struct Params {
   uint64_t timeout_ns;
   uint64_t off_cmat, off_cflag, off_dflag, off_free, off_local, off_data;
   int32_t* status_host;
+  uint64_t* trace;  // MOE_EP_TRACE_WORDS per CTA, or null
+};
+
+// Timeline hooks (no effect when the caller passed no trace buffer).
+#define TRACE_SET(p, i, v)                                                     \
+  do {                                                                         \
+    if ((p).trace) (p).trace[size_t(blockIdx.x) * MOE_EP_TRACE_WORDS + (i)] = (v); \
+  } while (0)
+#define TRACE_NOW(p) ((p).trace ? globaltimer_ns() : 0ull)
+
+struct RowMaps {
+  CUtensorMap m[kRowMaps];  // box {64, 8 << i}
 };
 
 // Local (never remote-accessed) words at off_local.
@@ -94,24 +127,30 @@ struct LocalWords {
 };
 
 struct Sched {
-  int ntiles_n, kblocks;
+  int nfeat, kblocks;
   int tiles_total, push_total, zero_total;
-  int cnt[kMaxCells];             // [src][le] rows this rank receives
-  int seg[kMaxCells + kMaxLocalExperts];  // [le][p], p = 0..W: compact start of position p (seg[.][1] = 0)
-  int rbase[kMaxLocalExperts + 1];  // compact base row of expert le in this rank's receive buffer
-  int push_off[kMaxCells];        // [d][le] first destination row at rank d
-  int push_cnt[kMaxCells];        // [d][le] rows this rank sends to (d, le)
-  int push_pfx[kMaxCells + 1];    // prefix of push items over cells (p-1)*El + le
-  int tile_pfx[kMaxCells + 1];    // prefix of tiles over cells: local le, then El + (p-1)*El + le
-  int tile_mlo[kMaxCells];
+  int cnt[kMaxCells];                     // [src][le] rows this rank receives
+  int seg[kMaxCells + kMaxLocalExperts];  // [le][q], q = 0..W: compact start of position q (seg[.][1] = 0)
+  int rbase[kMaxLocalExperts + 1];        // compact base row of expert le in this rank's receive buffer
+  int loc_tr[kMaxLocalExperts];           // rows per local tile of expert le (multiple of 16)
+  int rem_tr[kMaxLocalExperts];           // rows per remote tile of expert le
+  int push_off[kMaxCells];                // [d][le] first destination row at rank d
+  int push_cnt[kMaxCells];                // [d][le] rows this rank sends to (d, le)
+  int push_pfx[kMaxCells + 1];            // prefix of push items over cells le*(W-1) + (q-1)
+  int tile_pfx[kMaxLocalExperts + 1];     // prefix of tiles over experts
+  int loc_nt[kMaxLocalExperts];           // local row tiles of expert le
+  int rem_nt[kMaxLocalExperts];           // remote row tiles of expert le
+  int tmp[kMaxCells];                     // scratch while building
 };
 
 struct Smem {
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
-  uint64_t tfull[2];
-  uint64_t tempty[2];
+  uint64_t full[kStages];   // leader: both CTAs' bytes for the stage landed
+  uint64_t empty[kStages];  // each CTA: the pair MMA finished reading the stage
+  uint64_t tfull[2];        // each CTA: accumulator ready
+  uint64_t tempty[2];       // leader: both CTAs' epilogues drained the accumulator
+  uint64_t go[kGoSlots];    // peer: the leader's verdict for a tile
   uint64_t drain;
+  uint32_t go_verdict[kGoSlots];
   uint32_t tmem_base;
   int abort_flag;
   int push_item;
@@ -123,6 +162,12 @@ __device__ __forceinline__ uint32_t* at_u32(unsigned char* base, uint64_t off) {
   return reinterpret_cast<uint32_t*>(base + off);
 }
 
+__device__ __forceinline__ bool aborted(Smem& sm) {
+  return *reinterpret_cast<volatile int*>(&sm.abort_flag) != 0;
+}
+
+// Latch the first error (device word + mapped host word) and stop both CTAs
+// of the pair.
 __device__ void raise_error(const Params& p, Smem& sm, int code, int site, int detail) {
   LocalWords* lw = reinterpret_cast<LocalWords*>(p.local + p.off_local);
   const uint32_t w = status_word(code, site, detail);
@@ -133,10 +178,7 @@ __device__ void raise_error(const Params& p, Smem& sm, int code, int site, int d
     __threadfence_system();
   }
   atomicExch(&sm.abort_flag, 1);
-}
-
-__device__ __forceinline__ bool aborted(Smem& sm) {
-  return *reinterpret_cast<volatile int*>(&sm.abort_flag) != 0;
+  st_shared_cluster_u32(mapa_shared(smem_u32(&sm.abort_flag), cluster_ctarank() ^ 1u), 1u);
 }
 
 // Wait until a flag written by a peer reaches `epoch` (wrap-safe compare).
@@ -155,10 +197,10 @@ __device__ bool wait_epoch(const uint32_t* flag, uint32_t epoch, uint64_t timeou
 
 // Bounded mbarrier wait; pipeline waits only end early on abort or after a
 // hard bound well above the peer timeout (a bug guard).
-__device__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t bound_ns, Smem& sm) {
+__device__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t bound_ns, Smem& sm, bool cluster_scope = false) {
   uint64_t deadline = 0;
   for (uint32_t spin = 0;; ++spin) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (cluster_scope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
     if ((spin & 63) == 63) {
       if (aborted(sm)) return false;
       const uint64_t now = globaltimer_ns();
@@ -180,148 +222,188 @@ __device__ __forceinline__ int find_cell(const int* pfx, int ncells, int t) {
 }
 
 struct Tile {
-  int le, m, n, remote;
+  int le, feat, remote;
+  int row0, row1;  // rows [row0, row1) of the expert's local slot or compact remote rows
+  int n;           // MMA N: row1 - row0 rounded up to 16
 };
 
-__device__ __forceinline__ Tile decode_tile(const Sched& s, int W, int El, int t) {
-  const int ncells = W * El;
-  const int c = find_cell(s.tile_pfx, ncells, t);
+// Tiles are expert-major: expert le's cell holds nfeat feature slices, each
+// followed by all of its row tiles (local first, then remote), so the tiles
+// that share a weight slice run back to back on neighbouring clusters and
+// read it once from HBM.
+__device__ __forceinline__ Tile decode_tile(const Sched& s, int W, int El, int me, int t) {
+  const int c = find_cell(s.tile_pfx, El, t);
   const int r = t - s.tile_pfx[c];
-  Tile tile;
-  tile.remote = c >= El;
-  tile.le = tile.remote ? (c - El) % El : c;
-  tile.m = s.tile_mlo[c] + r / s.ntiles_n;
-  tile.n = r % s.ntiles_n;
-  return tile;
+  const int nrt = s.loc_nt[c] + s.rem_nt[c];
+  Tile tl;
+  tl.le = c;
+  tl.feat = r / nrt;
+  int i = r % nrt;
+  tl.remote = i >= s.loc_nt[c];
+  if (tl.remote) i -= s.loc_nt[c];
+  const int rows = tl.remote ? s.seg[tl.le * (W + 1) + W] : s.cnt[me * El + tl.le];
+  const int tr = tl.remote ? s.rem_tr[tl.le] : s.loc_tr[tl.le];
+  tl.row0 = i * tr;
+  tl.row1 = min(tl.row0 + tr, rows);
+  tl.n = (tl.row1 - tl.row0 + 15) & ~15;
+  return tl;
 }
 
-// m-tile index of the first tile whose last valid row is >= x (x < R).
-__device__ __forceinline__ int first_mtile_reaching(int x) { return x < BM ? 0 : (x - (BM - 1) + BM - 1) / BM; }
+// Rows per tile for `rows` rows: the fewest tiles of at most 256 rows,
+// balanced, rounded up to a multiple of 16.
+__device__ __forceinline__ int tile_rows(int rows) {
+  if (rows <= 0) return 16;
+  const int nt = (rows + kMaxTileRows - 1) / kMaxTileRows;
+  return ((rows + nt - 1) / nt + 15) & ~15;
+}
+
+// In-place exclusive scan of a[0..n) by one warp; a[n] receives the total.
+__device__ void warp_exclusive_scan(int* a, int n, int lane) {
+  int carry = 0;
+  for (int base = 0; base < n; base += 32) {
+    const int i = base + lane;
+    const int v = i < n ? a[i] : 0;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (i < n) a[i] = carry + x - v;
+    carry += __shfl_sync(0xffffffffu, x, 31);
+  }
+  if (lane == 0) a[n] = carry;
+  __syncwarp();
+}
 
 // Build the schedule for this call from the full count matrix.  All ranks
 // hold identical matrices, so every validation failure is seen by all ranks.
+// Every step is parallel over (rank, expert) cells; prefix sums are warp
+// scans over shared memory.
 __device__ void build_schedule(const Params& p, Sched& s, Smem& sm) {
   const int W = p.W, El = p.El, me = p.me, tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
   const uint32_t par = p.epoch & 1u;
   const int32_t* cm = reinterpret_cast<const int32_t*>(p.local + p.off_cmat) + size_t(par) * W * W * El;
   // cmat[owner][src][le]: rows src sends to owner's local expert le.
   auto C = [&](int owner, int src, int le) { return cm[(size_t(owner) * W + src) * El + le]; };
+  const int nfeat = (p.N + kFeatPair - 1) / kFeatPair;
 
   if (tid == 0) {
-    s.ntiles_n = (p.N + BN - 1) / BN;
+    s.nfeat = nfeat;
     s.kblocks = (p.H + BK - 1) / BK;
+    s.zero_total = W * El;
   }
-  for (int i = tid; i < W * El; i += kThreads) {
-    const int src = i / El, le = i % El;
-    s.cnt[i] = C(me, src, le);
-  }
-  __syncthreads();
-
   // Validation: 0 <= count <= gm everywhere, chunk slots suffice.
   for (int i = tid; i < W * W * El; i += kThreads) {
     const int v = cm[i];
-    if (v < 0 || int64_t(v) > p.gm || (v + p.push_rows - 1) / p.push_rows > p.max_chunks) {
+    if (v < 0 || int64_t(v) > p.gm || (v + p.push_rows - 1) / p.push_rows > p.max_chunks)
       raise_error(p, sm, kBadArg, kSiteTable, i);
-    }
   }
+  // Per (d, le): rows this rank receives from d (cnt), rows it sends to d
+  // (push_cnt), d's total remote rows for le (push_off, scanned below) and
+  // the rows that precede this rank's segment at d (tmp).
+  for (int i = tid; i < W * El; i += kThreads) {
+    const int d = i / El, le = i % El;
+    s.cnt[i] = C(me, d, le);
+    const int q_me = (me - d + W) % W;  // my position at d (0 means d == me)
+    int before = 0, total = 0;
+    for (int q = 1; q < W; ++q) {
+      const int v = C(d, (d + q) % W, le);
+      if (q < q_me) before += v;
+      total += v;
+    }
+    const int sc = (d == me) ? 0 : C(d, me, le);
+    s.push_cnt[i] = sc;
+    s.push_off[i] = total;
+    s.tmp[i] = before;
+    if (d != me) s.push_pfx[le * (W - 1) + (q_me - 1)] = (sc + p.push_rows - 1) / p.push_rows;
+  }
+  __syncthreads();
 
-  // Per local expert: compact segment starts (positions 1..W-1) and rows.
+  // Per local expert: compact segment starts (positions 1..W-1), tile sizes.
   for (int le = tid; le < El; le += kThreads) {
     int* sg = s.seg + le * (W + 1);
     sg[0] = 0;
-    sg[1] = 0;
     int run = 0;
     for (int q = 1; q < W; ++q) {
       sg[q] = run;
       run += s.cnt[((me + q) % W) * El + le];
     }
     sg[W] = run;
-  }
-  __syncthreads();
-  if (tid == 0) {
-    int run = 0;
-    for (int le = 0; le < El; ++le) {
-      s.rbase[le] = run;
-      run += s.seg[le * (W + 1) + W];
-    }
-    s.rbase[El] = run;
-  }
-  // Push offsets: where my rows for (d, le) land at rank d.
-  for (int d = tid; d < W; d += kThreads) {
-    const int q_me = (me - d + W) % W;  // my position at d (0 means d == me)
-    int base = 0;
-    for (int le = 0; le < El; ++le) {
-      int before = 0, total = 0;
-      for (int q = 1; q < W; ++q) {
-        const int v = C(d, (d + q) % W, le);
-        if (q < q_me) before += v;
-        total += v;
-      }
-      s.push_off[d * El + le] = base + before;
-      s.push_cnt[d * El + le] = (d == me) ? 0 : C(d, me, le);
-      base += total;
-    }
-    if (int64_t(base) > p.cap_rows) raise_error(p, sm, kCapacity, kSiteTable, d);
+    const int lr = s.cnt[me * El + le];
+    s.loc_tr[le] = tile_rows(lr);
+    s.rem_tr[le] = tile_rows(run);
+    s.loc_nt[le] = (lr + s.loc_tr[le] - 1) / s.loc_tr[le];
+    s.rem_nt[le] = (run + s.rem_tr[le] - 1) / s.rem_tr[le];
+    s.rbase[le] = run;                                   // scanned below
+    s.tile_pfx[le] = (s.loc_nt[le] + s.rem_nt[le]) * nfeat;  // scanned below
   }
   __syncthreads();
 
-  if (tid == 0) {
-    // Push items: positions p = 1..W-1 (destination d = me - p), experts, chunks.
-    int run = 0;
-    for (int q = 1; q < W; ++q) {
-      const int d = (me - q + W) % W;
-      for (int le = 0; le < El; ++le) {
-        s.push_pfx[(q - 1) * El + le] = run;
-        run += (s.push_cnt[d * El + le] + p.push_rows - 1) / p.push_rows;
-      }
+  // Prefix sums, one warp each:
+  //  * rbase: compact base of each expert in this rank's receive buffer;
+  //  * tile_pfx: tiles, expert-major (see decode_tile);
+  //  * push_pfx: push items, expert-major — experts, then positions
+  //    q = 1..W-1 (destination d = me - q), then row chunks.  Every sender
+  //    finishes an expert's rows for all destinations before the next
+  //    expert, matching the expert-major order of the receivers' tiles;
+  //  * push_off (per destination d, warps 3..): where my rows for (d, le)
+  //    land at d = d's compact base of le + the rows that precede mine.
+  if (warp == 0) warp_exclusive_scan(s.rbase, El, lane);
+  if (warp == 1) {
+    warp_exclusive_scan(s.tile_pfx, El, lane);
+    if (lane == 0) s.tiles_total = s.tile_pfx[El];
+  }
+  if (warp == 2) {
+    warp_exclusive_scan(s.push_pfx, El * (W - 1), lane);
+    if (lane == 0) s.push_total = s.push_pfx[El * (W - 1)];
+  }
+  for (int d = warp - 3; d >= 0 && d < W; d += kThreads / 32 - 3) {
+    int* row = s.push_off + d * El;
+    const int last = row[El - 1];
+    warp_exclusive_scan(row, El - 1, lane);  // row[El-1] receives the sum of the first El-1 totals
+    const int total = row[El - 1] + last;
+    __syncwarp();
+    for (int le = lane; le < El; le += 32) {
+      if (le == El - 1) row[le] = total - last;  // exclusive prefix of the last expert
     }
-    s.push_pfx[(W - 1) * El] = run;
-    s.push_total = run;
-    s.zero_total = W * El;
-
-    // Tiles: local cells first, then remote cells by the latest position
-    // their rows depend on, so work follows data arrival.
-    const int nn = s.ntiles_n;
-    int t = 0;
-    for (int le = 0; le < El; ++le) {
-      s.tile_pfx[le] = t;
-      s.tile_mlo[le] = 0;
-      t += ((s.cnt[me * El + le] + BM - 1) / BM) * nn;
-    }
-    for (int q = 1; q < W; ++q) {
-      for (int le = 0; le < El; ++le) {
-        const int c = El + (q - 1) * El + le;
-        const int* sg = s.seg + le * (W + 1);
-        const int R = sg[W];
-        const int mtiles = (R + BM - 1) / BM;
-        const int lo = sg[q] < R ? first_mtile_reaching(sg[q]) : mtiles;
-        const int hi = (q + 1 <= W - 1 && sg[q + 1] < R) ? first_mtile_reaching(sg[q + 1]) : mtiles;
-        const int lo_c = (sg[q] < sg[q + 1]) ? lo : hi;  // empty segment: no tiles
-        s.tile_pfx[c] = t;
-        s.tile_mlo[c] = lo_c;
-        t += (hi > lo_c ? hi - lo_c : 0) * nn;
-      }
-    }
-    s.tile_pfx[W * El] = t;
-    s.tiles_total = t;
+    __syncwarp();
+    for (int le = lane; le < El; le += 32) row[le] += s.tmp[d * El + le];
+    if (lane == 0 && int64_t(total) > p.cap_rows) raise_error(p, sm, kCapacity, kSiteTable, d);
   }
   __syncthreads();
 }
 
+__device__ __forceinline__ int64_t out_row_of(const Sched& s, const Params& p, const Tile& tl, int row) {
+  const int W = p.W;
+  if (!tl.remote) return (int64_t(tl.le) * W + p.me) * p.gm + row;
+  const int* sg = s.seg + tl.le * (W + 1);
+  int q = 1;
+  while (q < W - 1 && row >= sg[q + 1]) ++q;
+  const int src = (p.me + q) % W;
+  return (int64_t(tl.le) * W + src) * p.gm + (row - sg[q]);
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
-    fused_ep_kernel(const __grid_constant__ CUtensorMap tm_a_local, const __grid_constant__ CUtensorMap tm_a_remote,
-                    const __grid_constant__ CUtensorMap tm_b, const Params p) {
+    fused_ep_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ RowMaps rows_local,
+                    const __grid_constant__ RowMaps rows_remote, const Params p) {
   extern __shared__ unsigned char smem_dyn[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
   unsigned char* stage_mem = base;  // kStages * kStageBytes, 1024-aligned
-  Sched& s = *reinterpret_cast<Sched*>(base + kStages * kStageBytes);
-  Smem& sm = *reinterpret_cast<Smem*>(base + kStages * kStageBytes + sizeof(Sched));
+  unsigned char* epi_mem = base + kStages * kStageBytes;
+  Sched& s = *reinterpret_cast<Sched*>(epi_mem + kEpiStageBytes);
+  Smem& sm = *reinterpret_cast<Smem*>(epi_mem + kEpiStageBytes + sizeof(Sched));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
   const int W = p.W, El = p.El, me = p.me;
   const uint32_t par = p.epoch & 1u;
+  const uint32_t crank = cluster_ctarank();
+  const bool leader = crank == 0;
+  const uint32_t cid = cluster_id_x(), ncl = num_clusters_x();
   const uint64_t pipe_bound = 2 * p.timeout_ns + 1000000000ull;
   LocalWords* lw = reinterpret_cast<LocalWords*>(p.local + p.off_local);
+  if (tid == 0) TRACE_SET(p, MOE_EP_TRACE_START, TRACE_NOW(p));
 
   if (tid == 0) {
     for (int i = 0; i < kStages; ++i) {
@@ -332,22 +414,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sm.tfull[i], 1);
-      mbar_init(&sm.tempty[i], kEpiWarps);
+      mbar_init(&sm.tempty[i], 2 * kEpiWarps);
+    }
+    for (int i = 0; i < kGoSlots; ++i) {
+      mbar_init(&sm.go[i], 1);
+      sm.go_verdict[i] = 0;
     }
     mbar_init(&sm.drain, 1);
     sm.abort_flag = 0;
     fence_mbar_init();
-    prefetch_tensormap(&tm_a_local);
-    prefetch_tensormap(&tm_a_remote);
-    prefetch_tensormap(&tm_b);
+    prefetch_tensormap(&tm_w);
   }
+  cluster_sync();  // the peer's barriers exist before any remote arrive
   if (warp == kWarpMma) {
     __syncwarp();
-    tmem_alloc(&sm.tmem_base, kTmemCols);
-    tmem_relinquish();
+    tmem_alloc_pair(&sm.tmem_base, kTmemCols);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = sm.tmem_base;
 
@@ -378,164 +463,196 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
     }
+    TRACE_SET(p, MOE_EP_TRACE_COUNTS, TRACE_NOW(p));
   }
   __syncthreads();
   if (!aborted(sm)) build_schedule(p, s, sm);
   __syncthreads();
   const bool run_main = !aborted(sm);
+  if (tid == 0) TRACE_SET(p, MOE_EP_TRACE_SCHED, TRACE_NOW(p));
 
   if (run_main && warp == kWarpProducer) {
     if (lane == 0) {
-      uint32_t it = 0;
-      for (int t = blockIdx.x; t < s.tiles_total; t += gridDim.x) {
-        const Tile tl = decode_tile(s, W, El, t);
-        int arow;
-        const CUtensorMap* amap;
-        if (!tl.remote) {
-          arow = int((int64_t(me) * El + tl.le) * p.gm + int64_t(tl.m) * BM);
-          amap = &tm_a_local;
-        } else {
-          const int* sg = s.seg + tl.le * (W + 1);
-          const int R = sg[W];
-          const int r0 = tl.m * BM, r1 = min(r0 + BM, R);
-          bool ok = true;
-          for (int q = 1; q < W && ok; ++q) {
-            const int lo = max(r0, sg[q]), hi = min(r1, sg[q + 1]);
-            if (lo >= hi) continue;
-            const int src = (me + q) % W;
-            const uint32_t* fl = at_u32(p.local, p.off_dflag) + ((size_t(par) * W + src) * El + tl.le) * p.max_chunks;
-            for (int c = (lo - sg[q]) / p.push_rows; c <= (hi - 1 - sg[q]) / p.push_rows; ++c) {
-              if (!wait_epoch(fl + c, p.epoch, p.timeout_ns, sm)) {
-                raise_error(p, sm, kTimeout, kSiteTileFlag, src);
-                ok = false;
-                break;
+      const uint32_t bar_leader0 = mapa_shared(smem_u32(&sm.full[0]), 0);
+      uint32_t it = 0, ti = 0;
+      uint64_t flag_ns = 0, empty_ns = 0;
+      for (int t = int(cid); t < s.tiles_total; t += int(ncl), ++ti) {
+        const Tile tl = decode_tile(s, W, El, me, t);
+        const int slot = int(ti % kGoSlots);
+        if (leader) {
+          bool ok = !aborted(sm);
+          const uint64_t tw0 = TRACE_NOW(p);
+          if (ok && tl.remote) {
+            const int* sg = s.seg + tl.le * (W + 1);
+            for (int q = 1; q < W && ok; ++q) {
+              const int lo = max(tl.row0, sg[q]), hi = min(tl.row1, sg[q + 1]);
+              if (lo >= hi) continue;
+              const int src = (me + q) % W;
+              const uint32_t* fl = at_u32(p.local, p.off_dflag) + ((size_t(par) * W + src) * El + tl.le) * p.max_chunks;
+              for (int c = (lo - sg[q]) / p.push_rows; c <= (hi - 1 - sg[q]) / p.push_rows; ++c) {
+                if (!wait_epoch(fl + c, p.epoch, p.timeout_ns, sm)) {
+                  if (!aborted(sm)) raise_error(p, sm, kTimeout, kSiteTileFlag, src);
+                  ok = false;
+                  break;
+                }
               }
             }
           }
+          flag_ns += TRACE_NOW(p) - tw0;
+          st_shared_cluster_u32(mapa_shared(smem_u32(&sm.go_verdict[slot]), 1), ok ? 1u : 0u);
+          mbar_arrive_cluster(mapa_shared(smem_u32(&sm.go[slot]), 1));
           if (!ok) break;
-          fence_proxy_async_global();
-          arow = int(int64_t(par) * p.cap_rows + s.rbase[tl.le] + r0);
-          amap = &tm_a_remote;
+        } else {
+          if (!mbar_wait(&sm.go[slot], (ti / kGoSlots) & 1, pipe_bound, sm, true)) break;
+          if (*reinterpret_cast<volatile uint32_t*>(&sm.go_verdict[slot]) == 0) break;
         }
-        const int n0 = tl.n * BN;
-        const int nb = min(4, (p.N - n0 + 63) / 64);
-        const uint32_t tx = kABytes + uint32_t(nb) * kBBoxBytes;
+        if (tl.remote) fence_proxy_async_global();
+        const int half = tl.n >> 1;
+        const int64_t row_base = tl.remote ? int64_t(par) * p.cap_rows + s.rbase[tl.le] + tl.row0 + crank * half
+                                           : (int64_t(me) * El + tl.le) * p.gm + tl.row0 + crank * half;
+        const RowMaps& rm = tl.remote ? rows_remote : rows_local;
+        // Feature boxes of 64 that exist (trailing features beyond N are not loaded).
+        const int f_mine = tl.feat * kFeatPair + int(crank) * kFeatCta;
+        const int f_peer = tl.feat * kFeatPair + int(crank ^ 1u) * kFeatCta;
+        const int nb_mine = max(0, min(2, (p.N - f_mine + 63) / 64));
+        const int nb_peer = max(0, min(2, (p.N - f_peer + 63) / 64));
+        const uint32_t b_bytes = uint32_t(half) * BK * 2;
+        const uint32_t tx = uint32_t(nb_mine + nb_peer) * kABox + 2 * b_bytes;
         bool stop = false;
         for (int kb = 0; kb < s.kblocks; ++kb, ++it) {
           const int st = it % kStages;
           const uint32_t round = it / kStages;
+          const uint64_t te0 = TRACE_NOW(p);
           if (!mbar_wait(&sm.empty[st], (round & 1) ^ 1, pipe_bound, sm)) {
+            if (!aborted(sm)) raise_error(p, sm, kTimeout, kSitePipe, 0);
             stop = true;
             break;
           }
+          empty_ns += TRACE_NOW(p) - te0;
           unsigned char* a_dst = stage_mem + st * kStageBytes;
           unsigned char* b_dst = a_dst + kABytes;
-          mbar_arrive_expect_tx(&sm.full[st], tx);
-          tma_load_2d(amap, &sm.full[st], a_dst, kb * BK, arow);
-          for (int j = 0; j < nb; ++j) tma_load_3d(&tm_b, &sm.full[st], b_dst + j * kBBoxBytes, n0 + 64 * j, kb * BK, tl.le);
+          const uint32_t bar = bar_leader0 + uint32_t(st) * sizeof(uint64_t);
+          if (leader) mbar_arrive_expect_tx(&sm.full[st], tx);
+          for (int j = 0; j < nb_mine; ++j)
+            tma_load_3d_pair(&tm_w, bar, a_dst + j * kABox, f_mine + 64 * j, kb * BK, tl.le);
+          int off = 0;
+#pragma unroll
+          for (int m = kRowMaps - 1; m >= 0; --m) {
+            const int h = 8 << m;
+            if (half & h) {
+              tma_load_2d_pair(&rm.m[m], bar, b_dst + off * (BK * 2), kb * BK, int(row_base + off));
+              off += h;
+            }
+          }
           sm.fills[st] += 1;
         }
         if (stop) break;
       }
+      TRACE_SET(p, MOE_EP_TRACE_PRODUCER_END, TRACE_NOW(p));
+      TRACE_SET(p, MOE_EP_TRACE_TILES, ti);
+      TRACE_SET(p, MOE_EP_TRACE_FLAG_WAIT, flag_ns);
+      TRACE_SET(p, MOE_EP_TRACE_EMPTY_WAIT, empty_ns);
     }
   } else if (run_main && warp == kWarpMma) {
-    if (lane == 0) {
-      uint32_t it = 0, local_tile = 0;
-      for (int t = blockIdx.x; t < s.tiles_total; t += gridDim.x, ++local_tile) {
-        const uint32_t acc = local_tile & 1;
-        const uint32_t use = local_tile >> 1;
-        if (!mbar_wait(&sm.tempty[acc], (use & 1) ^ 1, pipe_bound, sm)) break;
+    if (leader && lane == 0) {
+      uint32_t it = 0, lt = 0;
+      uint64_t full_ns = 0, acc_ns = 0, issue_ns = 0;
+      for (int t = int(cid); t < s.tiles_total; t += int(ncl), ++lt) {
+        const Tile tl = decode_tile(s, W, El, me, t);
+        const uint32_t acc = lt & 1, use = lt >> 1;
+        const uint64_t ta0 = TRACE_NOW(p);
+        if (!mbar_wait(&sm.tempty[acc], (use & 1) ^ 1, pipe_bound, sm, true)) break;
+        acc_ns += TRACE_NOW(p) - ta0;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kAccCols;
+        const uint32_t idesc = make_idesc_mn(/*bf16*/ 1, kFeatPair, uint32_t(tl.n), /*A MN-major*/ 1, /*B K-major*/ 0);
         bool stop = false;
         for (int kb = 0; kb < s.kblocks; ++kb, ++it) {
           const int st = it % kStages;
           const uint32_t round = it / kStages;
+          const uint64_t tf0 = TRACE_NOW(p);
           if (!mbar_wait(&sm.full[st], round & 1, pipe_bound, sm)) {
             stop = true;
             break;
           }
+          const uint64_t tf1 = TRACE_NOW(p);
+          full_ns += tf1 - tf0;
           tc_fence_after();
           const uint32_t a_addr = smem_u32(stage_mem + st * kStageBytes);
           const uint32_t b_addr = a_addr + kABytes;
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t ad = smem_desc_sw128(a_addr + k * 32, 16, 1024);
-            const uint64_t bd = smem_desc_sw128(b_addr + k * 2048, kBBoxBytes, 1024);
-            tc_mma_f16(d_tmem, ad, bd, kIdesc, (kb | k) != 0 ? 1u : 0u);
+            const uint64_t ad = smem_desc_sw128(a_addr + k * 2048, kABox, 1024);  // MN-major: 16 K = 2 x 8-row groups
+            const uint64_t bd = smem_desc_sw128(b_addr + k * 32, 16, 1024);       // K-major: 16 K = 32 bytes
+            tc_mma_f16_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
           }
-          tc_commit(&sm.empty[st]);
+          tc_commit_pair_mc(&sm.empty[st], 0x3);
           sm.cons[st] += 1;
+          issue_ns += TRACE_NOW(p) - tf1;
         }
         if (stop) break;
-        tc_commit(&sm.tfull[acc]);
+        tc_commit_pair_mc(&sm.tfull[acc], 0x3);
       }
+      TRACE_SET(p, MOE_EP_TRACE_MMA_END, TRACE_NOW(p));
+      TRACE_SET(p, MOE_EP_TRACE_FULL_WAIT, full_ns);
+      TRACE_SET(p, MOE_EP_TRACE_ACC_WAIT, acc_ns);
+      TRACE_SET(p, MOE_EP_TRACE_MMA_ISSUE, issue_ns);
+      TRACE_SET(p, MOE_EP_TRACE_KBLOCKS, it);
     }
   } else if (run_main && warp >= kWarpEpi0 && warp < kWarpPush0) {
     const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;
-    uint32_t local_tile = 0;
-    for (int t = blockIdx.x; t < s.tiles_total; t += gridDim.x, ++local_tile) {
-      const Tile tl = decode_tile(s, W, El, t);
-      const uint32_t acc = local_tile & 1;
-      const uint32_t use = local_tile >> 1;
+    __nv_bfloat16* stage = reinterpret_cast<__nv_bfloat16*>(epi_mem) + (warp - kWarpEpi0) * 32 * 32;
+    const uint32_t tempty_leader = mapa_shared(smem_u32(&sm.tempty[0]), 0);
+    uint32_t lt = 0;
+    uint64_t epi_ns = 0;
+    for (int t = int(cid); t < s.tiles_total; t += int(ncl), ++lt) {
+      const Tile tl = decode_tile(s, W, El, me, t);
+      const uint32_t acc = lt & 1, use = lt >> 1;
+      const uint64_t tp0 = TRACE_NOW(p);
       if (!mbar_wait(&sm.tfull[acc], use & 1, pipe_bound, sm)) break;
+      epi_ns += TRACE_NOW(p) - tp0;
       tc_fence_after();
-      // Output row of this thread's accumulator lane (-1: not a valid row).
-      int64_t orow = -1;
-      if (!tl.remote) {
-        const int m = tl.m * BM + row;
-        if (m < s.cnt[me * El + tl.le]) orow = int64_t(tl.le) * W * p.gm + int64_t(me) * p.gm + m;
-      } else {
-        const int* sg = s.seg + tl.le * (W + 1);
-        const int r = tl.m * BM + row;
-        if (r < sg[W]) {
-          int q = 1;
-          while (q < W - 1 && r >= sg[q + 1]) ++q;
-          const int src = (me + q) % W;
-          orow = int64_t(tl.le) * W * p.gm + int64_t(src) * p.gm + (r - sg[q]);
-        }
-      }
-      const int n0 = tl.n * BN;
-      __nv_bfloat16* orow_ptr = p.out + (orow < 0 ? 0 : orow) * p.N;
-#pragma unroll 1
-      for (int j = 0; j < BN / 32; ++j) {
+      const int fbase = tl.feat * kFeatPair + int(crank) * kFeatCta + quarter * 32;
+      for (int jc = 0; jc * 32 < tl.n; ++jc) {
         uint32_t r[32];
         __syncwarp();
-        tmem_ld_32x32b_x32(tmem_base + acc * kAccCols + (uint32_t(quarter * 32) << 16) + j * 32, r);
+        tmem_ld_32x32b_x32(tmem_base + acc * kAccCols + (uint32_t(quarter * 32) << 16) + jc * 32, r);
         tmem_ld_wait();
-        if (orow >= 0) {
+        // stage[i][lane] = D[feature fbase + lane][row jc*32 + i]
 #pragma unroll
-          for (int c8 = 0; c8 < 4; ++c8) {
-            const int col = n0 + j * 32 + c8 * 8;
-            if (col + 8 <= p.N) {
-              uint4 v;
-              __nv_bfloat162 h0 = __floats2bfloat162_rn(__uint_as_float(r[c8 * 8 + 0]), __uint_as_float(r[c8 * 8 + 1]));
-              __nv_bfloat162 h1 = __floats2bfloat162_rn(__uint_as_float(r[c8 * 8 + 2]), __uint_as_float(r[c8 * 8 + 3]));
-              __nv_bfloat162 h2 = __floats2bfloat162_rn(__uint_as_float(r[c8 * 8 + 4]), __uint_as_float(r[c8 * 8 + 5]));
-              __nv_bfloat162 h3 = __floats2bfloat162_rn(__uint_as_float(r[c8 * 8 + 6]), __uint_as_float(r[c8 * 8 + 7]));
-              v.x = *reinterpret_cast<uint32_t*>(&h0);
-              v.y = *reinterpret_cast<uint32_t*>(&h1);
-              v.z = *reinterpret_cast<uint32_t*>(&h2);
-              v.w = *reinterpret_cast<uint32_t*>(&h3);
-              *reinterpret_cast<uint4*>(orow_ptr + col) = v;
-            }
+        for (int i = 0; i < 32; ++i) stage[i * 32 + lane] = __float2bfloat16_rn(__uint_as_float(r[i]));
+        __syncwarp();
+#pragma unroll
+        for (int step = 0; step < 4; ++step) {
+          const int c = lane + 32 * step;
+          const int i = c >> 2, part = c & 3;
+          const int row = tl.row0 + jc * 32 + i;
+          const int f = fbase + part * 8;
+          if (row < tl.row1 && f + 8 <= p.N) {
+            const uint4 v = *reinterpret_cast<const uint4*>(stage + i * 32 + part * 8);
+            *reinterpret_cast<uint4*>(p.out + out_row_of(s, p, tl, row) * p.N + f) = v;
           }
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.tempty[acc]);
+      if (lane == 0) mbar_arrive_cluster(tempty_leader + acc * sizeof(uint64_t));
+    }
+    if (warp == kWarpEpi0 && lane == 0) {
+      TRACE_SET(p, MOE_EP_TRACE_EPI_END, TRACE_NOW(p));
+      TRACE_SET(p, MOE_EP_TRACE_EPI_WAIT, epi_ns);
     }
   } else if (run_main && warp >= kWarpPush0) {
     const int pt = tid - kWarpPush0 * 32;
     const size_t row_bytes = size_t(p.H) * 2;
+    uint64_t items = 0, bytes = 0;
+    bool pushes_done = false;
     for (;;) {
       if (pt == 0) {
         int it = aborted(sm) ? 0x7fffffff : int(atomicAdd(&lw->push_ctr[par], 1u));
         if (it < s.push_total && p.epoch > 2) {
           const int c = find_cell(s.push_pfx, (W - 1) * El, it);
-          const int d = (me - (c / El + 1) + W) % W;
+          const int d = (me - (c % (W - 1) + 1) + W) % W;
           if (!wait_epoch(at_u32(p.local, p.off_free) + d, p.epoch - 2, p.timeout_ns, sm)) {
             raise_error(p, sm, kTimeout, kSiteFree, d);
             it = 0x7fffffff;
@@ -548,7 +665,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       named_bar_sync(kNamedBarPush, kPushThreads);
       if (item < s.push_total) {
         const int c = find_cell(s.push_pfx, (W - 1) * El, item);
-        const int q = c / El + 1, le = c % El;
+        const int q = c % (W - 1) + 1, le = c / (W - 1);
         const int d = (me - q + W) % W;
         const int chunk = item - s.push_pfx[c];
         const int j0 = chunk * p.push_rows;
@@ -575,8 +692,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (pt == 0) {
           uint32_t* fl = at_u32(peer, p.off_dflag) + ((size_t(par) * W + me) * El + le) * p.max_chunks + chunk;
           st_release_sys(fl, p.epoch);
+          items += 1;
+          bytes += uint64_t(nvec) * 16;
         }
       } else if (item < s.push_total + s.zero_total) {
+        if (pt == 0 && !pushes_done) {
+          pushes_done = true;
+          TRACE_SET(p, MOE_EP_TRACE_PUSH_END, TRACE_NOW(p));
+        }
         const int z = item - s.push_total;
         const int le = z / W, src = z % W;
         const int64_t c0 = s.cnt[src * El + le];
@@ -588,11 +711,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
     }
+    if (pt == 0) {
+      if (!pushes_done) TRACE_SET(p, MOE_EP_TRACE_PUSH_END, TRACE_NOW(p));
+      TRACE_SET(p, MOE_EP_TRACE_ZERO_END, TRACE_NOW(p));
+      TRACE_SET(p, MOE_EP_TRACE_PUSH_ITEMS, items);
+      TRACE_SET(p, MOE_EP_TRACE_PUSH_BYTES, bytes);
+    }
   }
 
   // ---- teardown: drain in-flight copies and MMAs, free TMEM, publish "free".
   __syncthreads();
-  if (tid == 0) {
+  if (aborted(sm) && !leader && tid == 0) {
+    // Pair loads issued by this CTA complete on the leader's barrier; after an
+    // abort give them time to land before the pair tears down (bug guard).
+    const uint64_t until = globaltimer_ns() + 200000ull;
+    while (globaltimer_ns() < until) {
+    }
+  }
+  cluster_sync();
+  if (leader && tid == 0) {
     for (int i = 0; i < kStages; ++i) {
       if (sm.fills[i] != sm.cons[i]) {
         // A fill that the MMA warp never consumed (abort): wait for its bytes.
@@ -607,8 +744,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   }
-  if (warp == kWarpMma && lane == 0) {
-    tc_commit(&sm.drain);
+  if (leader && warp == kWarpMma && lane == 0) {
+    tc_commit_pair(&sm.drain);
     const uint64_t deadline = globaltimer_ns() + 1000000000ull;
     while (!mbar_try_wait(&sm.drain, 0)) {
       if (globaltimer_ns() > deadline) {
@@ -618,11 +755,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();
   tc_fence_after();
   if (warp == kWarpMma) {
     __syncwarp();
-    tmem_dealloc(tmem_base, kTmemCols);
+    tmem_dealloc_pair(tmem_base, kTmemCols);
   }
   if (tid == 0) {
     __threadfence();
@@ -638,6 +775,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   }
+  if (tid == 0) TRACE_SET(p, MOE_EP_TRACE_END, TRACE_NOW(p));
+  cluster_sync();  // neither CTA leaves while its peer may still address it
 }
 
 // ------------------------------------------------------------------ host side
@@ -690,7 +829,15 @@ static int encode_3d(CUtensorMap* m, const void* ptr, uint64_t d0, uint64_t d1, 
   return r == CUDA_SUCCESS ? kOk : kCudaErr;
 }
 
-size_t fused_smem_bytes() { return 1024 + size_t(kStages) * kStageBytes + sizeof(Sched) + sizeof(Smem); }
+static int encode_rows(RowMaps* rm, const void* ptr, uint64_t H, uint64_t rows) {
+  for (int i = 0; i < kRowMaps; ++i)
+    if (encode_2d(&rm->m[i], ptr, H, rows, H * 2, BK, 8u << i)) return kCudaErr;
+  return kOk;
+}
+
+size_t fused_smem_bytes() {
+  return 1024 + size_t(kStages) * kStageBytes + kEpiStageBytes + sizeof(Sched) + sizeof(Smem);
+}
 
 int launch_fused(const moe_ep_run_params* a, cudaStream_t stream) {
   const int W = a->world_size, El = a->local_experts;
@@ -703,30 +850,28 @@ int launch_fused(const moe_ep_run_params* a, cudaStream_t stream) {
   if ((reinterpret_cast<uintptr_t>(a->tokens) | reinterpret_cast<uintptr_t>(a->weights) |
        reinterpret_cast<uintptr_t>(a->out)) & 15)
     return kBadArg;
+  if (a->num_ctas & 1u) return kBadArg;  // CTA pairs
   const int64_t rows_in = int64_t(W) * El * a->gm;
-  if (rows_in + BM > (int64_t(1) << 31) || 2 * a->cap_rows + BM > (int64_t(1) << 31)) return kBadArg;
+  if (rows_in + kMaxTileRows > (int64_t(1) << 31) || 2 * a->cap_rows + kMaxTileRows > (int64_t(1) << 31))
+    return kBadArg;
   if (!driver().ok) return kCudaErr;
 
   moe_ep_layout L;
   workspace_layout(W, El, a->hidden, a->elem_bytes, a->cap_rows, a->max_chunks, &L);
   unsigned char* local = reinterpret_cast<unsigned char*>(a->local_base);
 
-  CUtensorMap ta_local, ta_remote, tb;
+  CUtensorMap tw;
+  RowMaps rl, rr;
   const uint64_t H = uint64_t(a->hidden), N = uint64_t(a->out_dim);
-  if (rows_in == 0) {
-    // No rows at all: map a single dummy row so the descriptor stays valid.
-    if (encode_2d(&ta_local, a->tokens, H, 1, H * 2, BK, BM)) return kCudaErr;
-  } else if (encode_2d(&ta_local, a->tokens, H, uint64_t(rows_in), H * 2, BK, BM)) {
-    return kCudaErr;
-  }
-  // With no remote capacity (one rank) no remote tile exists; the map then
-  // describes the token buffer so that it never names unbacked memory.
+  if (encode_3d(&tw, a->weights, N, H, uint64_t(El), N * 2, H * N * 2, 64, BK)) return kCudaErr;
+  if (encode_rows(&rl, a->tokens, H, rows_in > 0 ? uint64_t(rows_in) : 1)) return kCudaErr;
+  // With no remote capacity (one rank) no remote tile exists; the maps then
+  // describe the token buffer so that they never name unbacked memory.
   if (a->cap_rows > 0) {
-    if (encode_2d(&ta_remote, local + L.off_data, H, uint64_t(2 * a->cap_rows), H * 2, BK, BM)) return kCudaErr;
+    if (encode_rows(&rr, local + L.off_data, H, uint64_t(2 * a->cap_rows))) return kCudaErr;
   } else {
-    ta_remote = ta_local;
+    rr = rl;
   }
-  if (encode_3d(&tb, a->weights, N, H, uint64_t(El), N * 2, H * N * 2, 64, BK)) return kCudaErr;
 
   Params p;
   p.W = W;
@@ -736,6 +881,7 @@ int launch_fused(const moe_ep_run_params* a, cudaStream_t stream) {
   p.N = a->out_dim;
   p.gm = a->gm;
   p.tokens = static_cast<const __nv_bfloat16*>(a->tokens);
+  p.weights = static_cast<const __nv_bfloat16*>(a->weights);
   p.recv_counts = a->recv_counts;
   p.out = static_cast<__nv_bfloat16*>(a->out);
   p.peers = a->peer_bases;
@@ -752,15 +898,34 @@ int launch_fused(const moe_ep_run_params* a, cudaStream_t stream) {
   p.off_local = L.off_local;
   p.off_data = L.off_data;
   p.status_host = a->status_host;
+  p.trace = a->trace;
 
-  int dev = 0, sms = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return kCudaErr;
-  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return kCudaErr;
-  const int grid = a->num_ctas > 0 ? int(a->num_ctas) : sms;
   const size_t smem = fused_smem_bytes();
   if (cudaFuncSetAttribute(fused_ep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
     return kCudaErr;
-  fused_ep_kernel<<<grid, kThreads, smem, stream>>>(ta_local, ta_remote, tb, p);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int grid = int(a->num_ctas);
+  if (grid == 0) {
+    int dev = 0, sms = 0, clusters = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return kCudaErr;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return kCudaErr;
+    cfg.gridDim = dim3(unsigned(sms & ~1), 1, 1);
+    if (cudaOccupancyMaxActiveClusters(&clusters, fused_ep_kernel, &cfg) != cudaSuccess || clusters < 1)
+      return kCudaErr;
+    grid = 2 * std::min(clusters, sms / 2);
+  }
+  cfg.gridDim = dim3(unsigned(grid), 1, 1);
+  if (cudaLaunchKernelEx(&cfg, fused_ep_kernel, tw, rl, rr, p) != cudaSuccess) return kCudaErr;
   return cudaGetLastError() == cudaSuccess ? kOk : kCudaErr;
 }
 
