@@ -22,7 +22,7 @@
 // memory and accumulates into each CTA's TMEM, so each CTA stages only 32 KB
 // per 64-wide k-block (a 6-stage ring).
 //
-// Warp roles (both CTAs of a pair, 320 threads):
+// Warp roles (both CTAs of a pair, 256 threads):
 //   warp 0      TMA producer.  The leader CTA waits for the arrival flags of
 //               the tile's rows and forwards a go/abort verdict to the peer;
 //               both then stream their halves; pair loads complete on the
@@ -32,7 +32,7 @@
 //   warps 2-5   epilogue: tcgen05.ld of this CTA's 128 features, bf16,
 //               transposed through shared memory, 16-byte stores of the valid
 //               rows to out[le, src*gm + m, :].
-//   warps 6-9   dispatch: copy this rank's valid rows for every peer straight
+//   warps 6-7   dispatch: copy this rank's valid rows for every peer straight
 //               into the peer's receive buffer over NVLink (16-byte vectors),
 //               then release a per-(src, expert, chunk) flag with the call's
 //               epoch; afterwards zero the padded output rows.
@@ -62,7 +62,7 @@ constexpr int kFeatPair = 256;                  // output features per pair tile
 constexpr int kFeatCta = 128;                   // features per CTA (TMEM lanes)
 constexpr int kMaxTileRows = 256;               // rows per tile (MMA N)
 constexpr int kEpiWarps = 4;
-constexpr int kPushWarps = 4;
+constexpr int kPushWarps = 2;                   // enough to stay ahead of the GEMM; more slow it down (L2 contention)
 constexpr int kWarpProducer = 0, kWarpMma = 1, kWarpEpi0 = 2, kWarpPush0 = 2 + kEpiWarps;
 constexpr int kThreads = (2 + kEpiWarps + kPushWarps) * 32;
 constexpr int kPushThreads = kPushWarps * 32;
@@ -835,6 +835,14 @@ static int encode_rows(RowMaps* rm, const void* ptr, uint64_t H, uint64_t rows) 
   return kOk;
 }
 
+// Per-device launch facts, computed on the first launch on each device.
+constexpr int kMaxDevices = 64;
+struct DeviceLaunchInfo {
+  bool ready;
+  int grid;
+};
+static DeviceLaunchInfo g_launch_info[kMaxDevices];
+
 size_t fused_smem_bytes() {
   return 1024 + size_t(kStages) * kStageBytes + kEpiStageBytes + sizeof(Sched) + sizeof(Smem);
 }
@@ -901,8 +909,9 @@ int launch_fused(const moe_ep_run_params* a, cudaStream_t stream) {
   p.trace = a->trace;
 
   const size_t smem = fused_smem_bytes();
-  if (cudaFuncSetAttribute(fused_ep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
-    return kCudaErr;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return kCudaErr;
+  DeviceLaunchInfo& info = g_launch_info[dev];
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -914,16 +923,20 @@ int launch_fused(const moe_ep_run_params* a, cudaStream_t stream) {
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  int grid = int(a->num_ctas);
-  if (grid == 0) {
-    int dev = 0, sms = 0, clusters = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return kCudaErr;
+  if (!info.ready) {
+    // Once per device: opt in to the shared memory size and size the
+    // persistent grid to the CTA pairs that can be resident together.
+    int sms = 0, clusters = 0;
+    if (cudaFuncSetAttribute(fused_ep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+      return kCudaErr;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return kCudaErr;
     cfg.gridDim = dim3(unsigned(sms & ~1), 1, 1);
     if (cudaOccupancyMaxActiveClusters(&clusters, fused_ep_kernel, &cfg) != cudaSuccess || clusters < 1)
       return kCudaErr;
-    grid = 2 * std::min(clusters, sms / 2);
+    info.grid = 2 * std::min(clusters, sms / 2);
+    info.ready = true;
   }
+  const int grid = a->num_ctas > 0 ? int(a->num_ctas) : info.grid;
   cfg.gridDim = dim3(unsigned(grid), 1, 1);
   if (cudaLaunchKernelEx(&cfg, fused_ep_kernel, tw, rl, rr, p) != cudaSuccess) return kCudaErr;
   return cudaGetLastError() == cudaSuccess ? kOk : kCudaErr;
