@@ -148,6 +148,28 @@ typedef struct moe_ep_run_params {
 
 int moe_ep_run(const moe_ep_run_params* params, void* stream);
 
+/* No counterpart in the reference.  The single-rank form of moe_ep_run for
+ * callers that cannot allocate device memory: a host that reaches the library
+ * only through this C ABI and owns no CUDA allocator, a process whose device
+ * memory is fixed after start-up, or a one-GPU user who does not want the
+ * exportable cuMem workspace that moe_ep_run needs.  The kernel's control
+ * words live in a fixed __device__ array inside the library
+ * (MOE_EP_NOALLOC_SCRATCH_BYTES on every GPU that loads it, held until the
+ * process exits); the caller still passes tokens, weights, recv_counts and
+ * out.  Requires world_size == 1 and rank == 0; peer_bases, local_base,
+ * cap_rows, push_rows, max_chunks and epoch are ignored.  More than
+ * MOE_EP_NOALLOC_MAX_EXPERTS local experts returns MOE_EP_SCRATCH_LIMIT.
+ * Allocates nothing: no cudaMalloc/cudaFree, no allocating library call.
+ * The first call on a device looks up the array's address and writes it
+ * synchronously, so make that call before any stream capture.  Every call
+ * reuses the same array and clears its control words first, so calls whose
+ * kernels overlap on the GPU (different streams, or several threads) race and
+ * must not be made; errors are reported through status_host. */
+#define MOE_EP_SCRATCH_LIMIT 6
+#define MOE_EP_NOALLOC_MAX_EXPERTS 64
+#define MOE_EP_NOALLOC_SCRATCH_BYTES 2048
+int moe_ep_run_noalloc(const moe_ep_run_params* params, void* stream);
+
 /* Copy the workspace status word to the host (synchronous). */
 int moe_ep_read_status(uint64_t local_base, const moe_ep_layout* layout, uint32_t* out);
 

@@ -12,15 +12,17 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libmoe_ep.so"
 
-OK, BAD_ARG, CUDA_ERR, TIMEOUT, CAPACITY, BAD_ROUTE = 0, 1, 2, 3, 4, 5
+OK, BAD_ARG, CUDA_ERR, TIMEOUT, CAPACITY, BAD_ROUTE, SCRATCH_LIMIT = 0, 1, 2, 3, 4, 5, 6
 STATUS_NAMES = {OK: "ok", BAD_ARG: "bad argument", CUDA_ERR: "CUDA error", TIMEOUT: "timed out waiting for a peer",
-                CAPACITY: "receive capacity exceeded", BAD_ROUTE: "bad routing input"}
+                CAPACITY: "receive capacity exceeded", BAD_ROUTE: "bad routing input",
+                SCRATCH_LIMIT: "size exceeds the fixed scratch of moe_ep_run_noalloc"}
+NOALLOC_MAX_EXPERTS = 64
 ABI_VERSION = 1
 
 # Every symbol include/moe_ep.h declares.
 EXPORTED = ["moe_ep_abi_version", "moe_ep_status_string", "moe_ep_num_sms", "moe_route", "moe_pack_padded",
             "moe_symm_alloc", "moe_symm_import", "moe_symm_free", "moe_ep_workspace_layout", "moe_ep_workspace_reset", "moe_ep_run",
-            "moe_ep_read_status"]
+            "moe_ep_read_status", "moe_ep_run_noalloc"]
 
 
 class MoeEpError(RuntimeError):
@@ -83,6 +85,7 @@ def lib() -> ctypes.CDLL:
     L.moe_ep_workspace_layout.argtypes = [c_int, c_int, c_i64, c_int, c_i64, c_int, P(Layout)]
     L.moe_ep_workspace_reset.argtypes = [c_u64, P(Layout), c_vp]
     L.moe_ep_run.argtypes = [P(RunParams), c_vp]
+    L.moe_ep_run_noalloc.argtypes = [P(RunParams), c_vp]
     L.moe_ep_read_status.argtypes = [c_u64, P(Layout), P(ctypes.c_uint32)]
     for name in EXPORTED:
         if name not in ("moe_ep_status_string",):

@@ -29,6 +29,7 @@ const char* moe_ep_status_string(int code) {
     case MOE_EP_TIMEOUT: return "timed out waiting for a peer";
     case MOE_EP_CAPACITY: return "receive capacity exceeded";
     case MOE_EP_BAD_ROUTE: return "bad routing input";
+    case MOE_EP_SCRATCH_LIMIT: return "size exceeds the fixed scratch of moe_ep_run_noalloc";
     default: return "unknown status";
   }
 }
