@@ -100,6 +100,7 @@ struct Params {
   unsigned char* local;
   int64_t cap_rows;
   int push_rows, max_chunks;
+  int w4;  // weights also described by the 4-D map (N % 128 == 0)
   uint32_t epoch;
   uint64_t timeout_ns;
   uint64_t off_cmat, off_cflag, off_dflag, off_free, off_local, off_data;
@@ -386,7 +387,8 @@ __device__ __forceinline__ int64_t out_row_of(const Sched& s, const Params& p, c
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-    fused_ep_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ RowMaps rows_local,
+    fused_ep_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_w4,
+                    const __grid_constant__ RowMaps rows_local,
                     const __grid_constant__ RowMaps rows_remote, const Params p) {
   extern __shared__ unsigned char smem_dyn[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
@@ -516,7 +518,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int f_peer = tl.feat * kFeatPair + int(crank ^ 1u) * kFeatCta;
         const int nb_mine = max(0, min(2, (p.N - f_mine + 63) / 64));
         const int nb_peer = max(0, min(2, (p.N - f_peer + 63) / 64));
-        const uint32_t b_bytes = uint32_t(half) * BK * 2;
+        // Rows go in one box of the smallest height >= half (rows past the
+        // tile land in unused shared memory).
+        int bm = 0;
+        while ((8 << bm) < half) ++bm;
+        const uint32_t b_bytes = uint32_t(8 << bm) * BK * 2;
         const uint32_t tx = uint32_t(nb_mine + nb_peer) * kABox + 2 * b_bytes;
         bool stop = false;
         for (int kb = 0; kb < s.kblocks; ++kb, ++it) {
@@ -533,17 +539,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           unsigned char* b_dst = a_dst + kABytes;
           const uint32_t bar = bar_leader0 + uint32_t(st) * sizeof(uint64_t);
           if (leader) mbar_arrive_expect_tx(&sm.full[st], tx);
-          for (int j = 0; j < nb_mine; ++j)
-            tma_load_3d_pair(&tm_w, bar, a_dst + j * kABox, f_mine + 64 * j, kb * BK, tl.le);
-          int off = 0;
-#pragma unroll
-          for (int m = kRowMaps - 1; m >= 0; --m) {
-            const int h = 8 << m;
-            if (half & h) {
-              tma_load_2d_pair(&rm.m[m], bar, b_dst + off * (BK * 2), kb * BK, int(row_base + off));
-              off += h;
-            }
+          // One 16 KB box for both 64-feature atoms when N is a multiple
+          // of 128, one box for the rows: the TMA engine overlaps few boxes
+          // at a time, so fewer, larger boxes keep more bytes in flight.
+          if (p.w4) {
+            if (nb_mine) tma_load_4d_pair(&tm_w4, bar, a_dst, 0, kb * BK, f_mine / 64, tl.le);
+          } else {
+            for (int j = 0; j < nb_mine; ++j)
+              tma_load_3d_pair(&tm_w, bar, a_dst + j * kABox, f_mine + 64 * j, kb * BK, tl.le);
           }
+          tma_load_2d_pair(&rm.m[bm], bar, b_dst, kb * BK, int(row_base));
           sm.fills[st] += 1;
         }
         if (stop) break;
@@ -829,6 +834,18 @@ static int encode_3d(CUtensorMap* m, const void* ptr, uint64_t d0, uint64_t d1, 
   return r == CUDA_SUCCESS ? kOk : kCudaErr;
 }
 
+static int encode_4d_atoms(CUtensorMap* m, const void* ptr, uint64_t N, uint64_t H, uint64_t El) {
+  const Driver& d = driver();
+  cuuint64_t dims[4] = {64, H, N / 64, El};
+  cuuint64_t strides[3] = {N * 2, 128, H * N * 2};
+  cuuint32_t box[4] = {64, uint32_t(BK), 2, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = d.cuTensorMapEncodeTiled(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(ptr), dims, strides,
+                                        box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? kOk : kCudaErr;
+}
+
 static int encode_rows(RowMaps* rm, const void* ptr, uint64_t H, uint64_t rows) {
   for (int i = 0; i < kRowMaps; ++i)
     if (encode_2d(&rm->m[i], ptr, H, rows, H * 2, BK, 8u << i)) return kCudaErr;
@@ -872,6 +889,11 @@ int launch_fused(const moe_ep_run_params* a, cudaStream_t stream) {
   RowMaps rl, rr;
   const uint64_t H = uint64_t(a->hidden), N = uint64_t(a->out_dim);
   if (encode_3d(&tw, a->weights, N, H, uint64_t(El), N * 2, H * N * 2, 64, BK)) return kCudaErr;
+  // Weights as (64 features, K, 64-feature atom, expert): one box holds both
+  // atoms of a CTA's 128 features.
+  CUtensorMap tw4 = tw;
+  const int w4 = (N % 128) == 0;
+  if (w4 && encode_4d_atoms(&tw4, a->weights, N, H, uint64_t(El))) return kCudaErr;
   if (encode_rows(&rl, a->tokens, H, rows_in > 0 ? uint64_t(rows_in) : 1)) return kCudaErr;
   // With no remote capacity (one rank) no remote tile exists; the maps then
   // describe the token buffer so that they never name unbacked memory.
@@ -896,6 +918,7 @@ int launch_fused(const moe_ep_run_params* a, cudaStream_t stream) {
   p.local = local;
   p.cap_rows = a->cap_rows;
   p.push_rows = a->push_rows;
+  p.w4 = w4;
   p.max_chunks = a->max_chunks;
   p.epoch = a->epoch;
   p.timeout_ns = a->timeout_ns;
@@ -938,7 +961,7 @@ int launch_fused(const moe_ep_run_params* a, cudaStream_t stream) {
   }
   const int grid = a->num_ctas > 0 ? int(a->num_ctas) : info.grid;
   cfg.gridDim = dim3(unsigned(grid), 1, 1);
-  if (cudaLaunchKernelEx(&cfg, fused_ep_kernel, tw, rl, rr, p) != cudaSuccess) return kCudaErr;
+  if (cudaLaunchKernelEx(&cfg, fused_ep_kernel, tw, tw4, rl, rr, p) != cudaSuccess) return kCudaErr;
   return cudaGetLastError() == cudaSuccess ? kOk : kCudaErr;
 }
 
