@@ -56,8 +56,9 @@
 
 namespace moe {
 
-constexpr int BK = 64;                          // k-block (bf16 elements, one 128-byte swizzle row)
-constexpr int kStages = 6;
+constexpr int BK = 64;                          // K of one 128-byte swizzle atom (bf16)
+constexpr int KB = 128;                         // K per pipeline stage (two atoms)
+constexpr int kStages = 3;
 constexpr int kFeatPair = 256;                  // output features per pair tile (MMA M)
 constexpr int kFeatCta = 128;                   // features per CTA (TMEM lanes)
 constexpr int kMaxTileRows = 256;               // rows per tile (MMA N)
@@ -66,10 +67,11 @@ constexpr int kPushWarps = 2;                   // enough to stay ahead of the G
 constexpr int kWarpProducer = 0, kWarpMma = 1, kWarpEpi0 = 2, kWarpPush0 = 2 + kEpiWarps;
 constexpr int kThreads = (2 + kEpiWarps + kPushWarps) * 32;
 constexpr int kPushThreads = kPushWarps * 32;
-constexpr uint32_t kABox = 64 * BK * 2;                       // 8 KB: 64 features x 64 K
-constexpr uint32_t kABytes = kFeatCta * BK * 2;               // 16 KB
-constexpr uint32_t kBBytesMax = (kMaxTileRows / 2) * BK * 2;  // 16 KB: 128 rows x 64 K
-constexpr uint32_t kStageBytes = kABytes + kBBytesMax;        // 32 KB
+constexpr uint32_t kABox = 64 * KB * 2;                       // 16 KB: 64 features x 128 K
+constexpr uint32_t kABytes = kFeatCta * KB * 2;               // 32 KB
+constexpr uint32_t kBHalf = (kMaxTileRows / 2) * BK * 2;      // 16 KB: 128 rows x 64 K
+constexpr uint32_t kBBytesMax = 2 * kBHalf;                   // 32 KB: 128 rows x 128 K
+constexpr uint32_t kStageBytes = kABytes + kBBytesMax;        // 64 KB
 constexpr int kMaxCells = 512;                  // W * El
 constexpr int kMaxLocalExperts = 256;
 constexpr uint32_t kAccCols = kMaxTileRows;
@@ -292,7 +294,7 @@ __device__ void build_schedule(const Params& p, Sched& s, Smem& sm) {
 
   if (tid == 0) {
     s.nfeat = nfeat;
-    s.kblocks = (p.H + BK - 1) / BK;
+    s.kblocks = (p.H + KB - 1) / KB;
     s.zero_total = W * El;
   }
   // Validation: 0 <= count <= gm everywhere, chunk slots suffice.
@@ -522,7 +524,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // tile land in unused shared memory).
         int bm = 0;
         while ((8 << bm) < half) ++bm;
-        const uint32_t b_bytes = uint32_t(8 << bm) * BK * 2;
+        const uint32_t b_bytes = 2 * uint32_t(8 << bm) * BK * 2;  // two 64-K halves
         const uint32_t tx = uint32_t(nb_mine + nb_peer) * kABox + 2 * b_bytes;
         bool stop = false;
         for (int kb = 0; kb < s.kblocks; ++kb, ++it) {
@@ -543,12 +545,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           // of 128, one box for the rows: the TMA engine overlaps few boxes
           // at a time, so fewer, larger boxes keep more bytes in flight.
           if (p.w4) {
-            if (nb_mine) tma_load_4d_pair(&tm_w4, bar, a_dst, 0, kb * BK, f_mine / 64, tl.le);
+            if (nb_mine) tma_load_4d_pair(&tm_w4, bar, a_dst, 0, kb * KB, f_mine / 64, tl.le);
           } else {
             for (int j = 0; j < nb_mine; ++j)
-              tma_load_3d_pair(&tm_w, bar, a_dst + j * kABox, f_mine + 64 * j, kb * BK, tl.le);
+              tma_load_3d_pair(&tm_w, bar, a_dst + j * kABox, f_mine + 64 * j, kb * KB, tl.le);
           }
-          tma_load_2d_pair(&rm.m[bm], bar, b_dst, kb * BK, int(row_base));
+          tma_load_2d_pair(&rm.m[bm], bar, b_dst, kb * KB, int(row_base));
+          tma_load_2d_pair(&rm.m[bm], bar, b_dst + kBHalf, kb * KB + BK, int(row_base));
           sm.fills[st] += 1;
         }
         if (stop) break;
@@ -586,9 +589,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t a_addr = smem_u32(stage_mem + st * kStageBytes);
           const uint32_t b_addr = a_addr + kABytes;
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
+          for (int k = 0; k < KB / 16; ++k) {
             const uint64_t ad = smem_desc_sw128(a_addr + k * 2048, kABox, 1024);  // MN-major: 16 K = 2 x 8-row groups
-            const uint64_t bd = smem_desc_sw128(b_addr + k * 32, 16, 1024);       // K-major: 16 K = 32 bytes
+            // K-major rows: 16 K = 32 bytes inside a 64-K atom; the second atom is kBHalf further.
+            const uint64_t bd = smem_desc_sw128(b_addr + (k >> 2) * kBHalf + (k & 3) * 32, 16, 1024);
             tc_mma_f16_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
           }
           tc_commit_pair_mc(&sm.empty[st], 0x3);
@@ -838,7 +842,7 @@ static int encode_4d_atoms(CUtensorMap* m, const void* ptr, uint64_t N, uint64_t
   const Driver& d = driver();
   cuuint64_t dims[4] = {64, H, N / 64, El};
   cuuint64_t strides[3] = {N * 2, 128, H * N * 2};
-  cuuint32_t box[4] = {64, uint32_t(BK), 2, 1};
+  cuuint32_t box[4] = {64, uint32_t(KB), 2, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = d.cuTensorMapEncodeTiled(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(ptr), dims, strides,
                                         box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -888,7 +892,7 @@ int launch_fused(const moe_ep_run_params* a, cudaStream_t stream) {
   CUtensorMap tw;
   RowMaps rl, rr;
   const uint64_t H = uint64_t(a->hidden), N = uint64_t(a->out_dim);
-  if (encode_3d(&tw, a->weights, N, H, uint64_t(El), N * 2, H * N * 2, 64, BK)) return kCudaErr;
+  if (encode_3d(&tw, a->weights, N, H, uint64_t(El), N * 2, H * N * 2, 64, KB)) return kCudaErr;
   // Weights as (64 features, K, 64-feature atom, expert): one box holds both
   // atoms of a CTA's 128 features.
   CUtensorMap tw4 = tw;
