@@ -19,14 +19,17 @@
 // not a whole 128-row M tile.  Two CTAs of a cluster form a pair: one
 // tcgen05.mma.cta_group::2 (M = 256 features, N = rows, K = 16) reads each
 // CTA's 128 features of A and half of the rows of B from that CTA's shared
-// memory and accumulates into each CTA's TMEM, so each CTA stages only 32 KB
-// per 64-wide k-block (a 6-stage ring).
+// memory and accumulates into each CTA's TMEM, so each CTA stages 64 KB per
+// 128-deep k-stage (3 stages).  Loads use few, large TMA boxes (one 32 KB box
+// for a CTA's weights per stage): the TMA engine overlaps a limited number of
+// boxes, so box size sets the bytes in flight.
 //
 // Warp roles (both CTAs of a pair, 256 threads):
-//   warp 0      TMA producer.  The leader CTA waits for the arrival flags of
-//               the tile's rows and forwards a go/abort verdict to the peer;
-//               both then stream their halves; pair loads complete on the
-//               leader's full barrier.
+//   warp 0      TMA producer.  The leader CTA takes the next tile from a
+//               global counter (dynamic scheduling), waits for the arrival
+//               flags of its rows and publishes it to every role of both
+//               CTAs; both then stream their halves; pair loads complete on
+//               the leader's full barrier.
 //   warp 1      MMA issuer (leader only): one thread issues the pair MMAs and
 //               commits to both CTAs' barriers.
 //   warps 2-5   epilogue: tcgen05.ld of this CTA's 128 features, bf16,
@@ -126,7 +129,8 @@ struct LocalWords {
   uint32_t push_ctr[2];
   uint32_t done_ctr[2];
   uint32_t status;
-  uint32_t pad[3];
+  uint32_t tile_ctr[2];
+  uint32_t pad;
 };
 
 struct Sched {
@@ -153,7 +157,7 @@ struct Smem {
   uint64_t tempty[2];       // leader: both CTAs' epilogues drained the accumulator
   uint64_t go[kGoSlots];    // peer: the leader's verdict for a tile
   uint64_t drain;
-  uint32_t go_verdict[kGoSlots];
+  int go_tile[kGoSlots];    // the tile the leader handed out for this slot, or -1 (stop)
   uint32_t tmem_base;
   int abort_flag;
   int push_item;
@@ -213,6 +217,14 @@ __device__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t bound_ns, Sme
   }
 }
 
+// The leader's producer hands tiles out dynamically: it takes the next tile
+// of the call from a global counter and publishes it, in slot ti % kGoSlots,
+// to both CTAs of the pair; every role of both CTAs reads the same sequence.
+// The leader runs at most kStages k-blocks ahead of its MMA, which runs at
+// most two tiles ahead of the epilogues, so kGoSlots slots are never
+// overwritten before all readers are past them.
+__device__ int wait_tile(Smem& sm, uint32_t ti, uint64_t bound_ns);
+
 __device__ __forceinline__ int find_cell(const int* pfx, int ncells, int t) {
   // largest c with pfx[c] <= t (pfx[0] = 0, pfx[ncells] = total > t)
   int lo = 0, hi = ncells - 1;
@@ -222,6 +234,12 @@ __device__ __forceinline__ int find_cell(const int* pfx, int ncells, int t) {
     else hi = mid - 1;
   }
   return lo;
+}
+
+__device__ int wait_tile(Smem& sm, uint32_t ti, uint64_t bound_ns) {
+  const int slot = int(ti % kGoSlots);
+  if (!mbar_wait(&sm.go[slot], (ti / kGoSlots) & 1, bound_ns, sm, true)) return -1;
+  return *reinterpret_cast<volatile int*>(&sm.go_tile[slot]);
 }
 
 struct Tile {
@@ -404,7 +422,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t par = p.epoch & 1u;
   const uint32_t crank = cluster_ctarank();
   const bool leader = crank == 0;
-  const uint32_t cid = cluster_id_x(), ncl = num_clusters_x();
   const uint64_t pipe_bound = 2 * p.timeout_ns + 1000000000ull;
   LocalWords* lw = reinterpret_cast<LocalWords*>(p.local + p.off_local);
   if (tid == 0) TRACE_SET(p, MOE_EP_TRACE_START, TRACE_NOW(p));
@@ -422,7 +439,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < kGoSlots; ++i) {
       mbar_init(&sm.go[i], 1);
-      sm.go_verdict[i] = 0;
+      sm.go_tile[i] = -1;
     }
     mbar_init(&sm.drain, 1);
     sm.abort_flag = 0;
@@ -480,11 +497,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t bar_leader0 = mapa_shared(smem_u32(&sm.full[0]), 0);
       uint32_t it = 0, ti = 0;
       uint64_t flag_ns = 0, empty_ns = 0;
-      for (int t = int(cid); t < s.tiles_total; t += int(ncl), ++ti) {
-        const Tile tl = decode_tile(s, W, El, me, t);
+      // The leader claims one tile ahead, so the counter's round trip
+      // overlaps the current tile's loads.
+      int claimed = leader ? int(atomicAdd(&lw->tile_ctr[par], 1u)) : -1;
+      for (;; ++ti) {
         const int slot = int(ti % kGoSlots);
+        int t;
+        Tile tl{};
         if (leader) {
-          bool ok = !aborted(sm);
+          t = (aborted(sm) || claimed >= s.tiles_total) ? -1 : claimed;
+          if (t >= 0) claimed = int(atomicAdd(&lw->tile_ctr[par], 1u));
+          bool ok = t >= 0;
+          if (ok) tl = decode_tile(s, W, El, me, t);
           const uint64_t tw0 = TRACE_NOW(p);
           if (ok && tl.remote) {
             const int* sg = s.seg + tl.le * (W + 1);
@@ -503,12 +527,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           flag_ns += TRACE_NOW(p) - tw0;
-          st_shared_cluster_u32(mapa_shared(smem_u32(&sm.go_verdict[slot]), 1), ok ? 1u : 0u);
-          mbar_arrive_cluster(mapa_shared(smem_u32(&sm.go[slot]), 1));
-          if (!ok) break;
+          if (!ok) t = -1;
+          for (uint32_t r = 0; r < 2; ++r) {
+            st_shared_cluster_u32(mapa_shared(smem_u32(&sm.go_tile[slot]), r), uint32_t(t));
+            mbar_arrive_cluster(mapa_shared(smem_u32(&sm.go[slot]), r));
+          }
+          if (t < 0) break;
         } else {
-          if (!mbar_wait(&sm.go[slot], (ti / kGoSlots) & 1, pipe_bound, sm, true)) break;
-          if (*reinterpret_cast<volatile uint32_t*>(&sm.go_verdict[slot]) == 0) break;
+          t = wait_tile(sm, ti, pipe_bound);
+          if (t < 0) break;
+          tl = decode_tile(s, W, El, me, t);
         }
         if (tl.remote) fence_proxy_async_global();
         const int half = tl.n >> 1;
@@ -565,7 +593,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (leader && lane == 0) {
       uint32_t it = 0, lt = 0;
       uint64_t full_ns = 0, acc_ns = 0, issue_ns = 0;
-      for (int t = int(cid); t < s.tiles_total; t += int(ncl), ++lt) {
+      for (;; ++lt) {
+        const int t = wait_tile(sm, lt, pipe_bound);
+        if (t < 0) break;
         const Tile tl = decode_tile(s, W, El, me, t);
         const uint32_t acc = lt & 1, use = lt >> 1;
         const uint64_t ta0 = TRACE_NOW(p);
@@ -614,7 +644,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tempty_leader = mapa_shared(smem_u32(&sm.tempty[0]), 0);
     uint32_t lt = 0;
     uint64_t epi_ns = 0;
-    for (int t = int(cid); t < s.tiles_total; t += int(ncl), ++lt) {
+    for (;; ++lt) {
+      const int t = wait_tile(sm, lt, pipe_bound);
+      if (t < 0) break;
       const Tile tl = decode_tile(s, W, El, me, t);
       const uint32_t acc = lt & 1, use = lt >> 1;
       const uint64_t tp0 = TRACE_NOW(p);
@@ -776,6 +808,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (old == gridDim.x - 1) {
       __threadfence();
       lw->push_ctr[par ^ 1] = 0;
+      lw->tile_ctr[par ^ 1] = 0;
       lw->done_ctr[par ^ 1] = 0;
       __threadfence();
       for (int q = 0; q < W; ++q) {
