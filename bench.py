@@ -1,6 +1,7 @@
 """Benchmark: fused MoE expert-parallel layer (dispatch + grouped GEMM).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+                    [--path dispatch_gemm|combine]
 
 One process per GPU (torchrun for N > 1).  A step is one call of the fused
 layer ``alltoall_persistent_gemm.run`` on this rank's padded, expert-major
@@ -14,6 +15,12 @@ through the public API from pinned host buffers (``e2e``), the reference's
 NCCL all_to_all_single + bmm on the same inputs, and the oracle's CPU time on
 the host cores (``cpu_baseline``).  ``--impl reference`` times the oracle (the
 CPU restatement of the reference path) on the host cores instead.
+
+``--path combine`` times the layer with its return path instead: the fused
+kernel in return mode (each output row stored into its source rank's return
+region over NVLink) plus the top-k combine kernel (``combine.run``), against
+NCCL all_to_all_single + bmm + the reverse all_to_all_single + a torch
+gather/weighted sum on the same inputs.
 """
 from __future__ import annotations
 
@@ -38,6 +45,7 @@ from nvshmem_testing_b200 import alltoall_persistent_gemm as apg  # noqa: E402
 from nvshmem_testing_b200 import utils, workloads  # noqa: E402
 
 METRIC = "fused dispatch+grouped-GEMM µs/layer & TFLOP/s, 1/2/4/8 B200 vs NCCL a2a+GEMM"
+METRIC_COMBINE = "fused dispatch+grouped-GEMM+return+top-k combine µs/layer & TFLOP/s vs NCCL a2a+GEMM+a2a+combine"
 NVLINK_GBS = 770.0          # measured peer copy per direction on this pool (nominal 900)
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
@@ -167,6 +175,24 @@ def nccl_a2a_bmm(tokens, chunk, world, weights):
     return torch.bmm(x, weights)
 
 
+def nccl_layer_combine(tokens, chunk, world, weights, ids, vals, slots):
+    """The same layer with the return path done the NCCL way: the baseline's
+    a2a + bmm, the reverse all_to_all_single of the [El, W*gm, N] outputs
+    back to the senders' padded layout, and a torch gather + top-k weighted
+    sum (fp32) per token."""
+    out = nccl_a2a_bmm(tokens, chunk, world, weights)
+    El, N = weights.shape[0], weights.shape[2]
+    gm = chunk // El
+    send = out.view(El, world, gm, N).permute(1, 0, 2, 3).reshape(world * El * gm, N)
+    back = torch.empty_like(send)
+    dist.all_to_all_single(back, send)
+    E = El * world
+    valid = (ids >= 0) & (ids < E) & (slots >= 0)
+    rows = torch.where(valid, ids * gm + slots, torch.zeros_like(ids))
+    w = torch.where(valid, vals.float(), torch.zeros_like(vals, dtype=torch.float32))
+    return (back[rows].float() * w[..., None]).sum(dim=1).to(torch.bfloat16)
+
+
 def time_device(fn, steps: int, warmup: int, sampler_device=None):
     sampler = ClockSampler(sampler_device) if sampler_device is not None else None
     for _ in range(warmup):
@@ -284,6 +310,140 @@ def run_reference_arm(args) -> int:
     return 0
 
 
+def run_combine_path(args) -> int:
+    """The layer with its return path (``combine.run``): one JSON line like
+    the default path's, with the NCCL a2a + bmm + reverse a2a + combine arm."""
+    from nvshmem_testing_b200 import combine
+
+    rank, world, local = init_dist(args.gpus)
+    dev = torch.device("cuda", local)
+    wl = workloads.get(args.workload, dtype=torch.bfloat16, **overrides(args))
+    El = wl.local_experts(world)
+    tokens = workloads.tokens(wl, rank, device=dev)
+    ids_cpu = workloads.top_idxs(wl, rank)
+    vals_cpu = workloads.top_vals(wl, rank)
+    ids, vals = ids_cpu.to(dev), vals_cpu.to(dev)
+    weights = workloads.weights(wl, rank, world, device=dev)
+    r = utils.route(ids, wl.E, with_slots=True)
+    gm = utils.global_max_count(r)
+    coalesced = utils.pack_padded(tokens, r, gm)
+    chunk = El * gm
+    counts = r.counts
+    recv_counts = utils.recv_counts_from(counts, world)
+    rc_cpu, c_cpu = recv_counts.cpu(), counts.cpu().view(world, El)
+    rows_in = int(rc_cpu.sum())
+    remote_in = rows_in - int(rc_cpu[rank].sum())
+    remote_out = int(c_cpu.sum()) - int(c_cpu[rank].sum())
+    flops_rank = 2.0 * rows_in * wl.H * wl.N
+    # NVLink per direction: rows out and expert outputs back, both ways.
+    link_out = remote_out * wl.H * 2 + remote_in * wl.N * 2
+    link_in = remote_in * wl.H * 2 + remote_out * wl.N * 2
+    nvlink_bytes = max(link_out, link_in)
+
+    def step():
+        return combine.run(rank, coalesced, chunk, world, weights, recv_counts, ids, vals, r.slots)
+
+    ours = step()
+    torch.cuda.synchronize()
+    ok = True
+    if not args.no_nccl:
+        ref = nccl_layer_combine(coalesced, chunk, world, weights, ids, vals, r.slots)
+        ok = bool(torch.allclose(ours.float(), ref.float(), rtol=1e-2, atol=1e-2))
+        del ref
+    del ours
+
+    ms, clocks = time_device(step, args.steps, args.warmup, sampler_device=local)
+    ms_max = max_over_ranks(ms)
+    flops_total = sum_over_ranks(flops_rank)
+    value = flops_total / (ms_max * 1e-3) / 1e12
+
+    nccl = None
+    if not args.no_nccl:
+        ms_n, _ = time_device(lambda: nccl_layer_combine(coalesced, chunk, world, weights, ids, vals, r.slots),
+                              max(args.steps // 3, 10), args.warmup)
+        ms_n = max_over_ranks(ms_n)
+        nccl = {"us_per_layer": ms_n * 1e3, "value": flops_total / (ms_n * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "what": "NCCL a2a + bmm over padded rows + reverse a2a + torch gather/top-k weighted sum"}
+
+    # end to end through the public API (combine.moe_layer) from pinned host buffers
+    x_host = workloads.tokens(wl, rank).pin_memory()
+    ids_host, vals_host = ids_cpu.pin_memory(), vals_cpu.pin_memory()
+    y_host = torch.empty((wl.T, wl.N), dtype=torch.bfloat16).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in (x_host, ids_host, vals_host))
+    d2h = y_host.numel() * y_host.element_size()
+
+    def e2e_step():
+        x = x_host.to(dev, non_blocking=True)
+        i = ids_host.to(dev, non_blocking=True)
+        v = vals_host.to(dev, non_blocking=True)
+        y_host.copy_(combine.moe_layer(x, i, v, weights), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    for _ in range(3):
+        e2e_step()
+    dist.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    e.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(s.elapsed_time(e) / args.e2e_steps)
+    dist.barrier()
+
+    peaks, peaks_src = load_peaks()
+    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    hbm_peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    K = ids.shape[1]
+    # weights once, every valid row once, remote rows read for sending and
+    # written by peers, every output row written once (return region, local
+    # or remote) and read once by the combine, ids/vals/slots and y.
+    rows_out_total = int(c_cpu.sum())
+    hbm_bytes = (El * wl.H * wl.N * 2 + rows_in * wl.H * 2 + (remote_in + remote_out) * wl.H * 2
+                 + rows_in * wl.N * 2 + rows_out_total * wl.N * 2 + wl.T * K * 16 + wl.T * wl.N * 2)
+    t_gemm_us = flops_rank / (peak * 1e12) * 1e6
+    t_hbm_us = hbm_bytes / (hbm_peak * 1e9) * 1e6
+    t_link_us = nvlink_bytes / (NVLINK_GBS * 1e9) * 1e6
+    roof_us = max_over_ranks(max(t_gemm_us, t_hbm_us, t_link_us))
+    if t_hbm_us > t_gemm_us:
+        bound, achieved, peak_v, unit = "hbm", hbm_bytes / (ms_max * 1e-3) / 1e9, hbm_peak, "GB/s"
+        peak_note = f"{peaks_src} hbm_gbs"
+    else:
+        bound, achieved, peak_v, unit = "tensor", flops_rank / (ms_max * 1e-3) / 1e12, peak, "TFLOP/s"
+        peak_note = f"{peaks_src} bf16_tflops (burst)"
+    line = {
+        "metric": METRIC_COMBINE, "path": "combine", "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max, "us_per_layer": ms_max * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded)",
+        "config": {"workload": wl.name + "+combine", "tokens_per_rank": wl.T, "hidden": wl.H, "experts": wl.E,
+                   "local_experts": El, "top_k": wl.K, "out_dim": wl.N, "routing": wl.routing, "gm": gm,
+                   "parallelism": f"ep{world}", "l2": "inputs larger than L2 (weights and tokens > 126 MB)"},
+        "parity_vs_nccl_allclose": ok,
+        "roofline": {"bound": bound, "achieved": achieved, "peak": peak_v, "unit": unit,
+                     "frac": achieved / peak_v, "peak_source": peak_note, "traffic": None,
+                     "algorithmic_hbm_bytes": hbm_bytes, "tensor_tflops": flops_rank / (ms_max * 1e-3) / 1e12,
+                     "bounds_us": {"tensor": t_gemm_us, "hbm": t_hbm_us, "nvlink": t_link_us},
+                     "layer_roofline_us": roof_us, "layer_frac": roof_us / (ms_max * 1e3),
+                     "nvlink_bytes_rank": nvlink_bytes},
+        "cpu_baseline": None,
+        "e2e": {"value": flops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "us_per_layer": e2e_ms * 1e3,
+                "what": "pinned host x+ids+vals -> combine.moe_layer (route, pack, count a2a, fused return, "
+                        "combine) -> pinned host y"},
+        "nccl_layer_combine": nccl,
+        "gpu_launches": 2 * args.steps,  # fused kernel + combine kernel per step
+        "clocks": clocks,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    from nvshmem_testing_b200 import symm
+    symm.release_all()
+    dist.destroy_process_group()
+    return 0
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
@@ -296,11 +456,15 @@ def main(argv=None) -> int:
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-nccl", action="store_true")
+    ap.add_argument("--path", choices=["dispatch_gemm", "combine"], default="dispatch_gemm",
+                    help="dispatch_gemm: the reference's path (default); combine: with return + top-k combine")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.path == "combine":
+        return run_combine_path(args)
 
     rank, world, local = init_dist(args.gpus)
     dev = torch.device("cuda", local)

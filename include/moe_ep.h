@@ -18,6 +18,11 @@
  *   moe_ep_run                  alltoall_persistent_gemm.py:207-309 (run:
  *                               peer copies + flags + fused grouped GEMM) and
  *                               baseline.py:8-56 (same output contract)
+ *   moe_route_slots,            the step after the reference's path: the
+ *   moe_ep_workspace_layout_ret, return of expert outputs to their source
+ *   moe_ep_run_combine          ranks and the top-k weighted sum with the
+ *                               router weights that utils.py:24-25 computes
+ *                               (top_vals) and the reference never uses
  */
 #ifndef MOE_EP_H
 #define MOE_EP_H
@@ -38,7 +43,7 @@ extern "C" {
 #define MOE_EP_CAPACITY 4
 #define MOE_EP_BAD_ROUTE 5
 
-#define MOE_EP_ABI_VERSION 1
+#define MOE_EP_ABI_VERSION 2
 
 int moe_ep_abi_version(void);
 const char* moe_ep_status_string(int code);
@@ -57,6 +62,14 @@ int moe_ep_num_sms(int device, int* out);
  * E <= 1024, K <= 32.  One CTA; suited to T up to ~10^5 tokens. */
 int moe_route(const void* top_idxs, int ids_are_int64, int64_t T, int K, int E, int32_t* counts, int32_t* offsets,
               int32_t* perm, int32_t* max_count, void* stream);
+
+/* moe_route plus, for the return path,
+ *   slots     [T, K] int32: j such that perm[offsets[e] + j] = t for
+ *                    e = top_idxs[t, k] (the token's row inside bucket e,
+ *                    i.e. padded send row e*gm + j); -1 where the id is
+ *                    outside [0, E) or repeats an earlier id of the row. */
+int moe_route_slots(const void* top_idxs, int ids_are_int64, int64_t T, int K, int E, int32_t* counts,
+                    int32_t* offsets, int32_t* perm, int32_t* slots, int32_t* max_count, void* stream);
 
 /* Replaces utils.py:54-69: out[e*gm + j, :] = tokens[perm[offsets[e] + j], :]
  * for j < counts[e] and zero rows for counts[e] <= j < gm.  Requires
@@ -83,10 +96,17 @@ typedef struct moe_ep_layout {
   uint64_t ctrl_bytes; /* bytes [0, ctrl_bytes) must start zeroed              */
   uint64_t off_data;   /* element [2][cap_rows][H]: compact remote rows        */
   uint64_t total_bytes;
+  uint64_t off_rflag;  /* uint32 [W peer]: last epoch the peer returned rows   */
+  uint64_t off_ret;    /* bf16 [ret_rows][ret_cols]: returned expert outputs   */
+  uint64_t ret_bytes;  /* 0 without a return region                            */
 } moe_ep_layout;
 
 int moe_ep_workspace_layout(int W, int El, int64_t H, int elem_bytes, int64_t cap_rows, int max_chunks,
                             moe_ep_layout* out);
+/* The same layout with a return region of ret_rows x ret_cols bf16 (for
+ * moe_ep_run_combine: ret_rows >= W*El*gm, ret_cols = out_dim). */
+int moe_ep_workspace_layout_ret(int W, int El, int64_t H, int elem_bytes, int64_t cap_rows, int max_chunks,
+                                int64_t ret_rows, int64_t ret_cols, moe_ep_layout* out);
 
 /* Zero the control region [0, ctrl_bytes) of a freshly allocated workspace
  * (counts, flags, epochs, counters).  Every rank must do this, and all ranks
@@ -169,6 +189,37 @@ int moe_ep_run(const moe_ep_run_params* params, void* stream);
 #define MOE_EP_NOALLOC_MAX_EXPERTS 64
 #define MOE_EP_NOALLOC_SCRATCH_BYTES 2048
 int moe_ep_run_noalloc(const moe_ep_run_params* params, void* stream);
+
+/* ---------------------------------------------------------------- return path
+ * The layer with its combine step (no counterpart in the reference, whose
+ * path ends at the expert outputs):
+ *   y[t, :] = sum over k of top_vals[t, k] * (x_t @ weights_e)
+ * for e = top_idxs[t, k] of this rank's tokens, counting each distinct valid
+ * id of a row once (like the routing) and skipping ids outside [0, E).
+ * One call launches the fused kernel of moe_ep_run in return mode — every
+ * output row is stored (bf16) into its source rank's return region over
+ * NVLink, at the row its padded send buffer holds the token in, and the
+ * last CTA releases a per-source flag — and then a combine kernel that
+ * waits (bounded by timeout_ns) for all W flags and forms y in fp32,
+ * rounded to bf16 (tokens with no valid id get a zero row).
+ * `run` is as for moe_ep_run except that run->out is not used; the
+ * workspace must have a return region (moe_ep_workspace_layout_ret) of
+ * ret_rows >= W*El*gm rows and out_dim columns.  Collective like moe_ep_run;
+ * all ranks use this call or moe_ep_run for the same epoch. */
+typedef struct moe_ep_combine_params {
+  const void* top_idxs;  /* [T, K] this rank's expert ids (the moe_route_slots input) */
+  const void* top_vals;  /* [T, K] router weights, fp32 (vals_are_bf16 = 0) or bf16   */
+  const int32_t* slots;  /* [T, K] from moe_route_slots                               */
+  void* y;               /* [T, out_dim] bf16                                         */
+  int64_t T;             /* tokens of this rank                                       */
+  int64_t ret_rows;      /* rows of the workspace's return region                     */
+  int32_t K;             /* ids per token, <= 32                                      */
+  int32_t ids_are_int64;
+  int32_t vals_are_bf16;
+  int32_t reserved;
+} moe_ep_combine_params;
+
+int moe_ep_run_combine(const moe_ep_run_params* run, const moe_ep_combine_params* combine, void* stream);
 
 /* Copy the workspace status word to the host (synchronous). */
 int moe_ep_read_status(uint64_t local_base, const moe_ep_layout* layout, uint32_t* out);

@@ -17,12 +17,13 @@ STATUS_NAMES = {OK: "ok", BAD_ARG: "bad argument", CUDA_ERR: "CUDA error", TIMEO
                 CAPACITY: "receive capacity exceeded", BAD_ROUTE: "bad routing input",
                 SCRATCH_LIMIT: "size exceeds the fixed scratch of moe_ep_run_noalloc"}
 NOALLOC_MAX_EXPERTS = 64
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 # Every symbol include/moe_ep.h declares.
 EXPORTED = ["moe_ep_abi_version", "moe_ep_status_string", "moe_ep_num_sms", "moe_route", "moe_pack_padded",
             "moe_symm_alloc", "moe_symm_import", "moe_symm_free", "moe_ep_workspace_layout", "moe_ep_workspace_reset", "moe_ep_run",
-            "moe_ep_read_status", "moe_ep_run_noalloc"]
+            "moe_ep_read_status", "moe_ep_run_noalloc", "moe_route_slots", "moe_ep_workspace_layout_ret",
+            "moe_ep_run_combine"]
 
 
 class MoeEpError(RuntimeError):
@@ -37,7 +38,8 @@ class MoeEpError(RuntimeError):
 class Layout(ctypes.Structure):
     _fields_ = [("off_cmat", ctypes.c_uint64), ("off_cflag", ctypes.c_uint64), ("off_dflag", ctypes.c_uint64),
                 ("off_free", ctypes.c_uint64), ("off_local", ctypes.c_uint64), ("ctrl_bytes", ctypes.c_uint64),
-                ("off_data", ctypes.c_uint64), ("total_bytes", ctypes.c_uint64)]
+                ("off_data", ctypes.c_uint64), ("total_bytes", ctypes.c_uint64), ("off_rflag", ctypes.c_uint64),
+                ("off_ret", ctypes.c_uint64), ("ret_bytes", ctypes.c_uint64)]
 
 
 class RunParams(ctypes.Structure):
@@ -48,6 +50,12 @@ class RunParams(ctypes.Structure):
                 ("local_base", ctypes.c_uint64), ("cap_rows", ctypes.c_int64), ("push_rows", ctypes.c_int32),
                 ("max_chunks", ctypes.c_int32), ("epoch", ctypes.c_uint32), ("num_ctas", ctypes.c_uint32),
                 ("timeout_ns", ctypes.c_uint64), ("status_host", ctypes.c_void_p), ("trace", ctypes.c_void_p)]
+
+
+class CombineParams(ctypes.Structure):
+    _fields_ = [("top_idxs", ctypes.c_void_p), ("top_vals", ctypes.c_void_p), ("slots", ctypes.c_void_p),
+                ("y", ctypes.c_void_p), ("T", ctypes.c_int64), ("ret_rows", ctypes.c_int64), ("K", ctypes.c_int32),
+                ("ids_are_int64", ctypes.c_int32), ("vals_are_bf16", ctypes.c_int32), ("reserved", ctypes.c_int32)]
 
 
 TRACE_WORDS = 24
@@ -78,14 +86,17 @@ def lib() -> ctypes.CDLL:
     L.moe_ep_status_string.argtypes = [c_int]
     L.moe_ep_num_sms.argtypes = [c_int, P(c_int)]
     L.moe_route.argtypes = [c_vp, c_int, c_i64, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp]
+    L.moe_route_slots.argtypes = [c_vp, c_int, c_i64, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]
     L.moe_pack_padded.argtypes = [c_vp, c_i64, c_int, c_vp, c_vp, c_vp, c_int, c_i64, c_vp, c_vp]
     L.moe_symm_alloc.argtypes = [c_int, c_sz, P(c_sz), P(c_u64), P(c_int), P(c_u64)]
     L.moe_symm_import.argtypes = [c_int, c_int, c_sz, P(c_u64), P(c_u64)]
     L.moe_symm_free.argtypes = [c_u64, c_sz, c_u64]
     L.moe_ep_workspace_layout.argtypes = [c_int, c_int, c_i64, c_int, c_i64, c_int, P(Layout)]
+    L.moe_ep_workspace_layout_ret.argtypes = [c_int, c_int, c_i64, c_int, c_i64, c_int, c_i64, c_i64, P(Layout)]
     L.moe_ep_workspace_reset.argtypes = [c_u64, P(Layout), c_vp]
     L.moe_ep_run.argtypes = [P(RunParams), c_vp]
     L.moe_ep_run_noalloc.argtypes = [P(RunParams), c_vp]
+    L.moe_ep_run_combine.argtypes = [P(RunParams), P(CombineParams), c_vp]
     L.moe_ep_read_status.argtypes = [c_u64, P(Layout), P(ctypes.c_uint32)]
     for name in EXPORTED:
         if name not in ("moe_ep_status_string",):
@@ -106,8 +117,9 @@ def decode_status_word(w: int) -> tuple[int, int, int]:
     return (w >> 24) & 0xFF, (w >> 16) & 0xFF, w & 0xFFFF
 
 
-def workspace_layout(W: int, El: int, H: int, elem_bytes: int, cap_rows: int, max_chunks: int) -> Layout:
+def workspace_layout(W: int, El: int, H: int, elem_bytes: int, cap_rows: int, max_chunks: int,
+                     ret_rows: int = 0, ret_cols: int = 0) -> Layout:
     L = Layout()
-    check(lib().moe_ep_workspace_layout(W, El, H, elem_bytes, cap_rows, max_chunks, ctypes.byref(L)),
-          "moe_ep_workspace_layout")
+    check(lib().moe_ep_workspace_layout_ret(W, El, H, elem_bytes, cap_rows, max_chunks, ret_rows, ret_cols,
+                                            ctypes.byref(L)), "moe_ep_workspace_layout_ret")
     return L

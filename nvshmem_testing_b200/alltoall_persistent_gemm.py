@@ -52,30 +52,15 @@ def raise_if_device_error(ws) -> None:
         raise N.MoeEpError(code, "moe_ep_run (device)", f"site={site} detail={detail}; the workspace is unusable")
 
 
-def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: int, hidden_dim: int,
-        num_experts: int, world_size: int, shmem=None, general_a2a: bool = False,
-        local_weights: torch.Tensor = None, recv_counts: torch.Tensor = None, *, group=None,
-        timeout_s: float | None = None, push_rows: int | None = None, num_ctas: int = 0,
-        check: bool = False, trace: torch.Tensor | None = None) -> torch.Tensor:
-    """Fused dispatch + grouped GEMM; see the module docstring.
+def _launch_params(me: int, W: int, tokens: torch.Tensor, transmit_size: int, hidden_dim: int,
+                   local_weights: torch.Tensor, recv_counts, group, timeout_s, push_rows, num_ctas, trace,
+                   ret_cols: int = 0):
+    """Validate the fused layer's inputs and fill ``moe_ep_run_params``.
 
-    Keyword-only extensions: ``group`` (process group, default WORLD),
-    ``timeout_s`` (bound on every device wait for a peer), ``push_rows``
-    (rows per NVLink chunk and arrival flag), ``num_ctas`` (0 = one per SM),
-    ``check`` (synchronise and raise on a device error before returning),
-    ``trace`` (int64 device tensor of at least ``num_sms * 24`` words that
-    receives the per-CTA device timeline, ``_native.TRACE_FIELDS``).
-    """
-    if general_a2a:
-        raise NotImplementedError("general/unbalanced a2a not implemented.")
-    assert dist.is_initialized()
-    assert tokens.is_cuda
-    assert tokens.shape[0] == transmit_size * world_size
+    Returns ``(workspace, params, (El, gm, N), keepalive)``; ``ret_cols`` > 0
+    selects a workspace with a return region (the combine path)."""
     if local_weights is None:
         raise ValueError("local_weights [El, H, N] is required")
-    me, W = _group_info(group, world_size, rank)
-    if W != world_size or me != rank:
-        raise ValueError(f"rank/world_size ({rank}/{world_size}) disagree with the process group ({me}/{W})")
     El, H, Nout = local_weights.shape
     if tokens.dim() != 2 or tokens.shape[1] != H or H != hidden_dim:
         raise ValueError(f"tokens {tuple(tokens.shape)} / hidden_dim {hidden_dim} do not match weights {tuple(local_weights.shape)}")
@@ -97,15 +82,14 @@ def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: in
         recv_counts = recv_counts.to(device=tokens.device, dtype=torch.int32).contiguous()
 
     rows = push_rows or DEFAULT_PUSH_ROWS
-    ws = get_workspace(W, El, H, gm, dev, group, me, rows)
+    ws = get_workspace(W, El, H, gm, dev, group, me, rows, ret_cols)
     raise_if_device_error(ws)
-    out = torch.empty((El, W * gm, Nout), dtype=torch.bfloat16, device=tokens.device)
 
     p = N.RunParams()
     p.world_size, p.rank, p.local_experts = W, me, El
     p.hidden, p.out_dim, p.elem_bytes, p.gm = H, Nout, 2, gm
     p.tokens, p.weights = tokens.data_ptr(), local_weights.data_ptr()
-    p.recv_counts, p.out = recv_counts.data_ptr(), out.data_ptr()
+    p.recv_counts = recv_counts.data_ptr()
     p.peer_bases, p.local_base = ws.peer_bases.data_ptr(), ws.base
     p.cap_rows, p.push_rows, p.max_chunks = ws.key.cap_rows, ws.push_rows, ws.key.max_chunks
     p.epoch = ws.next_epoch()
@@ -116,6 +100,35 @@ def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: in
         if trace.dtype != torch.int64 or not trace.is_cuda:
             raise TypeError("trace must be an int64 CUDA tensor")
         p.trace = trace.data_ptr()
+    return ws, p, (El, gm, Nout), (tokens, local_weights, recv_counts)
+
+
+def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: int, hidden_dim: int,
+        num_experts: int, world_size: int, shmem=None, general_a2a: bool = False,
+        local_weights: torch.Tensor = None, recv_counts: torch.Tensor = None, *, group=None,
+        timeout_s: float | None = None, push_rows: int | None = None, num_ctas: int = 0,
+        check: bool = False, trace: torch.Tensor | None = None) -> torch.Tensor:
+    """Fused dispatch + grouped GEMM; see the module docstring.
+
+    Keyword-only extensions: ``group`` (process group, default WORLD),
+    ``timeout_s`` (bound on every device wait for a peer), ``push_rows``
+    (rows per NVLink chunk and arrival flag), ``num_ctas`` (0 = one per SM),
+    ``check`` (synchronise and raise on a device error before returning),
+    ``trace`` (int64 device tensor of at least ``num_sms * 24`` words that
+    receives the per-CTA device timeline, ``_native.TRACE_FIELDS``).
+    """
+    if general_a2a:
+        raise NotImplementedError("general/unbalanced a2a not implemented.")
+    assert dist.is_initialized()
+    assert tokens.is_cuda
+    assert tokens.shape[0] == transmit_size * world_size
+    me, W = _group_info(group, world_size, rank)
+    if W != world_size or me != rank:
+        raise ValueError(f"rank/world_size ({rank}/{world_size}) disagree with the process group ({me}/{W})")
+    ws, p, (El, gm, Nout), keep = _launch_params(me, W, tokens, transmit_size, hidden_dim, local_weights,
+                                                 recv_counts, group, timeout_s, push_rows, num_ctas, trace)
+    out = torch.empty((El, W * gm, Nout), dtype=torch.bfloat16, device=tokens.device)
+    p.out = out.data_ptr()
     stream = torch.cuda.current_stream(tokens.device)
     N.check(N.lib().moe_ep_run(ctypes.byref(p), ctypes.c_void_p(stream.cuda_stream)), "moe_ep_run")
     if check:

@@ -4,11 +4,6 @@
 #include "moe_ep.h"
 #include "moe_ep_internal.h"
 
-namespace moe {
-int workspace_layout(int W, int El, int64_t H, int elem_bytes, int64_t cap_rows, int max_chunks, moe_ep_layout* L);
-int launch_fused(const moe_ep_run_params* a, cudaStream_t stream);
-}  // namespace moe
-
 using namespace moe;
 
 static int set_device(int device) {
@@ -45,7 +40,17 @@ int moe_route(const void* top_idxs, int ids_are_int64, int64_t T, int K, int E, 
       (T > 0 && !perm))
     return kBadArg;
   if (T * int64_t(K) >= (int64_t(1) << 31)) return kBadArg;
-  return launch_route(top_idxs, ids_are_int64, T, K, E, counts, offsets, perm, max_count,
+  return launch_route(top_idxs, ids_are_int64, T, K, E, counts, offsets, perm, nullptr, max_count,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int moe_route_slots(const void* top_idxs, int ids_are_int64, int64_t T, int K, int E, int32_t* counts,
+                    int32_t* offsets, int32_t* perm, int32_t* slots, int32_t* max_count, void* stream) {
+  if (T < 0 || K < 1 || K > kMaxRouteK || E < 1 || E > kMaxExperts || (T > 0 && (!top_idxs || !perm || !slots)) ||
+      !counts || !offsets || !max_count)
+    return kBadArg;
+  if (T * int64_t(K) >= (int64_t(1) << 31)) return kBadArg;
+  return launch_route(top_idxs, ids_are_int64, T, K, E, counts, offsets, perm, slots, max_count,
                       static_cast<cudaStream_t>(stream));
 }
 
@@ -164,12 +169,37 @@ int moe_symm_free(uint64_t ptr, size_t bytes, uint64_t handle) {
 int moe_ep_workspace_layout(int W, int El, int64_t H, int elem_bytes, int64_t cap_rows, int max_chunks,
                             moe_ep_layout* out) {
   if (W < 1 || El < 1 || H < 1 || elem_bytes < 1 || cap_rows < 0 || max_chunks < 1 || !out) return kBadArg;
-  return workspace_layout(W, El, H, elem_bytes, cap_rows, max_chunks, out);
+  return workspace_layout(W, El, H, elem_bytes, cap_rows, max_chunks, 0, 0, out);
+}
+
+int moe_ep_workspace_layout_ret(int W, int El, int64_t H, int elem_bytes, int64_t cap_rows, int max_chunks,
+                                int64_t ret_rows, int64_t ret_cols, moe_ep_layout* out) {
+  if (W < 1 || El < 1 || H < 1 || elem_bytes < 1 || cap_rows < 0 || max_chunks < 1 || ret_rows < 0 || ret_cols < 0 ||
+      !out)
+    return kBadArg;
+  return workspace_layout(W, El, H, elem_bytes, cap_rows, max_chunks, ret_rows, ret_cols, out);
 }
 
 int moe_ep_run(const moe_ep_run_params* params, void* stream) {
   if (!params) return kBadArg;
-  return launch_fused(params, static_cast<cudaStream_t>(stream));
+  return launch_fused(params, 0, static_cast<cudaStream_t>(stream));
+}
+
+int moe_ep_run_combine(const moe_ep_run_params* run, const moe_ep_combine_params* c, void* stream) {
+  if (!run || !c) return kBadArg;
+  if (c->T < 0 || c->K < 1 || c->K > kMaxRouteK || c->ret_rows <= 0 || (c->T > 0 && (!c->top_idxs || !c->top_vals ||
+      !c->slots || !c->y)))
+    return kBadArg;
+  if (reinterpret_cast<uintptr_t>(c->y) & 15) return kBadArg;
+  if (int64_t(run->world_size) * run->local_experts * run->gm > c->ret_rows) return kBadArg;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  moe_ep_layout L;
+  if (workspace_layout(run->world_size, run->local_experts, run->hidden, run->elem_bytes, run->cap_rows,
+                       run->max_chunks, c->ret_rows, run->out_dim, &L) != kOk)
+    return kBadArg;
+  const int rc = launch_fused(run, c->ret_rows, s);
+  if (rc != kOk) return rc;
+  return launch_combine(run, c, L, s);
 }
 
 int moe_ep_workspace_reset(uint64_t local_base, const moe_ep_layout* layout, void* stream) {

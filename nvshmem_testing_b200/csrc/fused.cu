@@ -84,16 +84,6 @@ constexpr int kRowMaps = 5;                     // B boxes of 8, 16, 32, 64, 128
 constexpr int kNamedBarPush = 1;
 constexpr uint32_t kEpiStageBytes = kEpiWarps * 32 * 32 * 2;  // 32 rows x 32 features bf16 per warp
 
-// Where an error was detected (status word "site" byte).
-enum Site : int {
-  kSiteCounts = 1,
-  kSiteTable = 2,
-  kSiteTileFlag = 3,
-  kSiteFree = 4,
-  kSitePipe = 5,
-  kSiteDrain = 6,
-};
-
 struct Params {
   int W, me, El, H, N;
   int64_t gm;
@@ -109,6 +99,11 @@ struct Params {
   uint32_t epoch;
   uint64_t timeout_ns;
   uint64_t off_cmat, off_cflag, off_dflag, off_free, off_local, off_data;
+  // Return mode (combine): instead of out, each output row goes to its
+  // source rank's return region, row (me*El + le)*gm + i, and the last CTA
+  // releases off_rflag[me] at every rank.
+  int ret;
+  uint64_t off_ret, off_rflag;
   int32_t* status_host;
   uint64_t* trace;  // MOE_EP_TRACE_WORDS per CTA, or null
 };
@@ -122,15 +117,6 @@ struct Params {
 
 struct RowMaps {
   CUtensorMap m[kRowMaps];  // box {64, 8 << i}
-};
-
-// Local (never remote-accessed) words at off_local.
-struct LocalWords {
-  uint32_t push_ctr[2];
-  uint32_t done_ctr[2];
-  uint32_t status;
-  uint32_t tile_ctr[2];
-  uint32_t pad;
 };
 
 struct Sched {
@@ -313,7 +299,7 @@ __device__ void build_schedule(const Params& p, Sched& s, Smem& sm) {
   if (tid == 0) {
     s.nfeat = nfeat;
     s.kblocks = (p.H + KB - 1) / KB;
-    s.zero_total = W * El;
+    s.zero_total = p.ret ? 0 : W * El;  // return mode writes no padded output
   }
   // Validation: 0 <= count <= gm everywhere, chunk slots suffice.
   for (int i = tid; i < W * W * El; i += kThreads) {
@@ -404,6 +390,21 @@ __device__ __forceinline__ int64_t out_row_of(const Sched& s, const Params& p, c
   while (q < W - 1 && row >= sg[q + 1]) ++q;
   const int src = (p.me + q) % W;
   return (int64_t(tl.le) * W + src) * p.gm + (row - sg[q]);
+}
+
+// Return mode: where output row `row` of tile tl goes — the source rank's
+// return region, at the row the source's padded send buffer holds it in.
+__device__ __forceinline__ unsigned char* ret_row_ptr(const Sched& s, const Params& p, const Tile& tl, int row) {
+  int src = p.me, i = row;
+  if (tl.remote) {
+    const int* sg = s.seg + tl.le * (p.W + 1);
+    int q = 1;
+    while (q < p.W - 1 && row >= sg[q + 1]) ++q;
+    src = (p.me + q) % p.W;
+    i = row - sg[q];
+  }
+  return reinterpret_cast<unsigned char*>(p.peers[src]) + p.off_ret +
+         ((int64_t(p.me) * p.El + tl.le) * p.gm + i) * int64_t(p.N) * 2;
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -671,7 +672,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int f = fbase + part * 8;
           if (row < tl.row1 && f + 8 <= p.N) {
             const uint4 v = *reinterpret_cast<const uint4*>(stage + i * 32 + part * 8);
-            *reinterpret_cast<uint4*>(p.out + out_row_of(s, p, tl, row) * p.N + f) = v;
+            if (p.ret) st_v4(ret_row_ptr(s, p, tl, row) + size_t(f) * 2, v);  // NVLink for remote rows
+            else *reinterpret_cast<uint4*>(p.out + out_row_of(s, p, tl, row) * p.N + f) = v;
           }
         }
       }
@@ -679,6 +681,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader + acc * sizeof(uint64_t));
     }
+    if (p.ret) fence_acq_rel_sys();  // this thread's return rows before the CTA's completion count
     if (warp == kWarpEpi0 && lane == 0) {
       TRACE_SET(p, MOE_EP_TRACE_EPI_END, TRACE_NOW(p));
       TRACE_SET(p, MOE_EP_TRACE_EPI_WAIT, epi_ns);
@@ -803,10 +806,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_dealloc_pair(tmem_base, kTmemCols);
   }
   if (tid == 0) {
-    __threadfence();
+    if (p.ret) __threadfence_system();
+    else __threadfence();
     const uint32_t old = atomicAdd(&lw->done_ctr[par], 1u);
     if (old == gridDim.x - 1) {
-      __threadfence();
+      if (p.ret) __threadfence_system();
+      else __threadfence();
       lw->push_ctr[par ^ 1] = 0;
       lw->tile_ctr[par ^ 1] = 0;
       lw->done_ctr[par ^ 1] = 0;
@@ -814,6 +819,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int q = 0; q < W; ++q) {
         unsigned char* peer = reinterpret_cast<unsigned char*>(p.peers[q]);
         st_release_sys(at_u32(peer, p.off_free) + me, p.epoch);
+      }
+      // Every CTA's return rows are out: tell each source rank.  After an
+      // error nothing is released and the sources' combine waits time out.
+      if (p.ret && ld_volatile_u32(&lw->status) == 0) {
+        for (int q = 0; q < W; ++q) {
+          unsigned char* peer = reinterpret_cast<unsigned char*>(p.peers[q]);
+          st_release_sys(at_u32(peer, p.off_rflag) + me, p.epoch);
+        }
       }
     }
   }
@@ -825,7 +838,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-int workspace_layout(int W, int El, int64_t H, int elem_bytes, int64_t cap_rows, int max_chunks, moe_ep_layout* L) {
+int workspace_layout(int W, int El, int64_t H, int elem_bytes, int64_t cap_rows, int max_chunks, int64_t ret_rows,
+                     int64_t ret_cols, moe_ep_layout* L) {
   size_t off = 0;
   L->off_cmat = off;
   off = align_up(off + size_t(2) * W * W * El * 4, 256);
@@ -834,13 +848,18 @@ int workspace_layout(int W, int El, int64_t H, int elem_bytes, int64_t cap_rows,
   L->off_dflag = off;
   off = align_up(off + size_t(2) * W * El * max_chunks * 4, 256);
   L->off_free = off;
-  off = align_up(off + size_t(W) * 4, 256);
+  L->off_rflag = off + align_up(size_t(W) * 4, 16);  // same 256-byte block for W <= 31
+  off = align_up(L->off_rflag + size_t(W) * 4, 256);
   L->off_local = off;
   off = align_up(off + sizeof(LocalWords), 256);
   L->ctrl_bytes = off;
   off = align_up(off, 4096);
   L->off_data = off;
   off += size_t(2) * cap_rows * H * elem_bytes;
+  off = align_up(off, 4096);
+  L->off_ret = off;
+  L->ret_bytes = size_t(ret_rows) * size_t(ret_cols) * 2;
+  off += L->ret_bytes;
   L->total_bytes = align_up(off, 4096);
   return kOk;
 }
@@ -901,14 +920,20 @@ size_t fused_smem_bytes() {
   return 1024 + size_t(kStages) * kStageBytes + kEpiStageBytes + sizeof(Sched) + sizeof(Smem);
 }
 
-int launch_fused(const moe_ep_run_params* a, cudaStream_t stream) {
+// ret_rows > 0 selects return mode: output rows go to the source ranks'
+// return regions (ret_rows rows of out_dim bf16 each, at least W*El*gm) and
+// `out` is not used.
+int launch_fused(const moe_ep_run_params* a, int64_t ret_rows, cudaStream_t stream) {
   const int W = a->world_size, El = a->local_experts;
   if (W < 1 || W > 64 || a->rank < 0 || a->rank >= W || El < 1 || El > kMaxLocalExperts || W * El > kMaxCells)
     return kBadArg;
   if (a->elem_bytes != 2 || a->hidden <= 0 || a->out_dim <= 0 || a->hidden % 8 || a->out_dim % 8 || a->gm < 0)
     return kBadArg;
   if (a->push_rows <= 0 || a->max_chunks <= 0 || a->cap_rows < 0 || a->epoch == 0) return kBadArg;
-  if (!a->tokens || !a->weights || !a->out || !a->peer_bases || !a->local_base || !a->recv_counts) return kBadArg;
+  const bool ret = ret_rows > 0;
+  if (!a->tokens || !a->weights || (!ret && !a->out) || !a->peer_bases || !a->local_base || !a->recv_counts)
+    return kBadArg;
+  if (ret && ret_rows < int64_t(W) * El * a->gm) return kBadArg;
   if ((reinterpret_cast<uintptr_t>(a->tokens) | reinterpret_cast<uintptr_t>(a->weights) |
        reinterpret_cast<uintptr_t>(a->out)) & 15)
     return kBadArg;
@@ -919,7 +944,7 @@ int launch_fused(const moe_ep_run_params* a, cudaStream_t stream) {
   if (!driver().ok) return kCudaErr;
 
   moe_ep_layout L;
-  workspace_layout(W, El, a->hidden, a->elem_bytes, a->cap_rows, a->max_chunks, &L);
+  workspace_layout(W, El, a->hidden, a->elem_bytes, a->cap_rows, a->max_chunks, ret ? ret_rows : 0, a->out_dim, &L);
   unsigned char* local = reinterpret_cast<unsigned char*>(a->local_base);
 
   CUtensorMap tw;
@@ -965,6 +990,9 @@ int launch_fused(const moe_ep_run_params* a, cudaStream_t stream) {
   p.off_free = L.off_free;
   p.off_local = L.off_local;
   p.off_data = L.off_data;
+  p.ret = ret;
+  p.off_ret = L.off_ret;
+  p.off_rflag = L.off_rflag;
   p.status_host = a->status_host;
   p.trace = a->trace;
 

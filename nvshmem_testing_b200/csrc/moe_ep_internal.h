@@ -6,6 +6,8 @@
 #include <cstddef>
 #include <cstdint>
 
+#include "moe_ep.h"
+
 namespace moe {
 
 // Status codes; identical to the MOE_EP_* values of include/moe_ep.h.
@@ -18,13 +20,33 @@ enum : int {
   kBadRoute = 5,
 };
 
+// Status-word sites shared by the kernels (the "site" byte of a latched error).
+enum Site : int {
+  kSiteCounts = 1,
+  kSiteTable = 2,
+  kSiteTileFlag = 3,
+  kSiteFree = 4,
+  kSitePipe = 5,
+  kSiteDrain = 6,
+  kSiteReturn = 7,
+};
+
 constexpr int kMaxExperts = 1024;  // routing kernel: experts per call
 constexpr int kMaxRouteK = 32;     // routing kernel: ids per token (top-k width)
 
 // ---- routing (route.cu)
 size_t route_smem_bytes(int E);
 int launch_route(const void* ids, int ids_are_int64, int64_t T, int K, int E, int32_t* counts, int32_t* offsets,
-                 int32_t* perm, int32_t* max_count, cudaStream_t stream);
+                 int32_t* perm, int32_t* slots, int32_t* max_count, cudaStream_t stream);
+// Words at the workspace's off_local (never accessed by peers).
+struct LocalWords {
+  uint32_t push_ctr[2];
+  uint32_t done_ctr[2];
+  uint32_t status;
+  uint32_t tile_ctr[2];
+  uint32_t pad;
+};
+
 int launch_pack_padded(const void* tokens, int64_t H, int elem_bytes, const int32_t* counts, const int32_t* offsets,
                        const int32_t* perm, int E, int64_t gm, void* out, int num_sms, cudaStream_t stream);
 
@@ -49,5 +71,11 @@ struct Driver {
 const Driver& driver();
 
 // ---- fused dispatch + grouped GEMM (fused.cu)
-struct RunArgs;  // mirrors moe_ep_run_params (include/moe_ep.h)
+int workspace_layout(int W, int El, int64_t H, int elem_bytes, int64_t cap_rows, int max_chunks, int64_t ret_rows,
+                     int64_t ret_cols, moe_ep_layout* L);
+int launch_fused(const moe_ep_run_params* a, int64_t ret_rows, cudaStream_t stream);
+
+// ---- return path: top-k weighted combine (combine.cu)
+int launch_combine(const moe_ep_run_params* run, const moe_ep_combine_params* c, const moe_ep_layout& L,
+                   cudaStream_t stream);
 }  // namespace moe

@@ -24,11 +24,6 @@
 #include "moe_ep.h"
 #include "moe_ep_internal.h"
 
-namespace moe {
-int workspace_layout(int W, int El, int64_t H, int elem_bytes, int64_t cap_rows, int max_chunks, moe_ep_layout* L);
-int launch_fused(const moe_ep_run_params* a, cudaStream_t stream);
-}  // namespace moe
-
 using namespace moe;
 
 namespace {
@@ -72,7 +67,7 @@ extern "C" int moe_ep_run_noalloc(const moe_ep_run_params* params, void* stream)
   // One flag slot per expert: a chunk of gm rows covers every valid count.
   const int push_rows = params->gm > 0 ? int(params->gm) : 1;
   moe_ep_layout L;
-  if (workspace_layout(1, params->local_experts, params->hidden, params->elem_bytes, 0, 1, &L) != kOk)
+  if (workspace_layout(1, params->local_experts, params->hidden, params->elem_bytes, 0, 1, 0, 0, &L) != kOk)
     return kBadArg;
   if (kPeerTableBytes + L.ctrl_bytes > kScratchBytes) return MOE_EP_SCRATCH_LIMIT;
 
@@ -94,5 +89,5 @@ extern "C" int moe_ep_run_noalloc(const moe_ep_run_params* params, void* stream)
   q.push_rows = push_rows;
   q.max_chunks = 1;
   q.epoch = 1;
-  return launch_fused(&q, s);
+  return launch_fused(&q, 0, s);
 }

@@ -1,5 +1,6 @@
 // Routing kernels: per-expert counts, expert offsets, the stable token
-// permutation, and the padded expert-major pack.
+// permutation (and, optionally, each (token, k)'s index inside its bucket, the
+// key of the return path), and the padded expert-major pack.
 //
 // These restate, on the device, the host loop of the reference's router
 // post-processing (utils.py:28-69):
@@ -62,7 +63,8 @@ __device__ int block_exclusive_scan(int v, int* warp_sums, int* total) {
 template <typename IdT>
 __global__ void __launch_bounds__(kRouteThreads, 1)
     route_kernel(const IdT* __restrict__ ids, int64_t T, int K, int E, int32_t* __restrict__ counts,
-                 int32_t* __restrict__ offsets, int32_t* __restrict__ perm, int32_t* __restrict__ max_count) {
+                 int32_t* __restrict__ offsets, int32_t* __restrict__ perm, int32_t* __restrict__ slots,
+                 int32_t* __restrict__ max_count) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   int* cnt = reinterpret_cast<int*>(smem_raw);                       // [E]
   int* cursor = cnt + E;                                             // [E]
@@ -102,6 +104,7 @@ __global__ void __launch_bounds__(kRouteThreads, 1)
       offsets[e] = carry + ex;
       cursor[e] = carry + ex;
       counts[e] = v;
+      cnt[e] = carry + ex;  // from here on: the expert's offset
     }
     carry += scan_total;
     __syncthreads();
@@ -151,10 +154,14 @@ __global__ void __launch_bounds__(kRouteThreads, 1)
         const int e = seen[k];
         bool dup = false;
         for (int j = 0; j < k; ++j) dup |= (seen[j] == e);
-        if (e < 0 || dup) continue;
+        if (e < 0 || dup) {
+          if (slots) slots[t * K + k] = -1;
+          continue;
+        }
         const size_t s = size_t(w) * E + e;
         const int pos = cursor[e] + wpre[s] + __popc(bits[s] & below);
         perm[pos] = static_cast<int32_t>(t);
+        if (slots) slots[t * K + k] = pos - cnt[e];  // index inside bucket e
       }
     }
     __syncthreads();
@@ -192,19 +199,19 @@ __global__ void pack_padded_kernel(const uint4* __restrict__ tokens, int64_t row
 size_t route_smem_bytes(int E) { return size_t(E) * (4 + 4 + 4 * kRouteWords + 2 * kRouteWords); }
 
 int launch_route(const void* ids, int ids_are_int64, int64_t T, int K, int E, int32_t* counts, int32_t* offsets,
-                 int32_t* perm, int32_t* max_count, cudaStream_t stream) {
+                 int32_t* perm, int32_t* slots, int32_t* max_count, cudaStream_t stream) {
   const size_t smem = route_smem_bytes(E);
   cudaError_t err;
   if (ids_are_int64) {
     err = cudaFuncSetAttribute(route_kernel<long long>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (err != cudaSuccess) return kCudaErr;
     route_kernel<long long><<<1, kRouteThreads, smem, stream>>>(static_cast<const long long*>(ids), T, K, E, counts,
-                                                              offsets, perm, max_count);
+                                                              offsets, perm, slots, max_count);
   } else {
     err = cudaFuncSetAttribute(route_kernel<int32_t>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (err != cudaSuccess) return kCudaErr;
     route_kernel<int32_t><<<1, kRouteThreads, smem, stream>>>(static_cast<const int32_t*>(ids), T, K, E, counts,
-                                                            offsets, perm, max_count);
+                                                            offsets, perm, slots, max_count);
   }
   return cudaGetLastError() == cudaSuccess ? kOk : kCudaErr;
 }

@@ -14,7 +14,8 @@ c10d store.  Here each rank
 4. publishes the table of W base addresses to the device.
 
 The region holds the per-parity count matrix, arrival flags, "free" epochs
-and the compact receive rows (``moe_ep_layout``).  Workspaces are cached by
+and the compact receive rows (``moe_ep_layout``), and for the combine path a
+return region that peers store expert outputs into.  Workspaces are cached by
 (W, El, H, capacity, device, group) like the reference's cache key
 (alltoall_persistent_gemm.py:161-163).
 """
@@ -101,6 +102,8 @@ class WorkspaceKey:
     push_rows: int
     device: int
     group: str
+    ret_rows: int = 0  # return region (combine): rows of ret_cols bf16 outputs
+    ret_cols: int = 0
 
 
 class SymmetricWorkspace:
@@ -113,7 +116,8 @@ class SymmetricWorkspace:
         self.rank = rank
         self.world = key.W
         self.push_rows = key.push_rows
-        self.layout = N.workspace_layout(key.W, key.El, key.H, 2, key.cap_rows, key.max_chunks)
+        self.layout = N.workspace_layout(key.W, key.El, key.H, 2, key.cap_rows, key.max_chunks, key.ret_rows,
+                                         key.ret_cols)
         dev = key.device
         mapped = ctypes.c_size_t()
         base = ctypes.c_uint64()
@@ -187,21 +191,25 @@ def group_name(group) -> str:
 
 
 def get_workspace(W: int, El: int, H: int, gm: int, device: int, group, rank: int,
-                  push_rows: int) -> SymmetricWorkspace:
+                  push_rows: int, ret_cols: int = 0) -> SymmetricWorkspace:
     """Cached workspace large enough for padded slots of `gm` rows.
 
     The remote receive capacity is (W-1)*El*gm rows (every remote slot full),
     i.e. the reference's padded receive buffer without this rank's own slot.
     Capacity is rounded up to a power of two in gm so that calls whose gm
     differs slightly reuse one workspace; all ranks see the same gm (it is the
-    all-reduced maximum), so all ranks make the same choice.
+    all-reduced maximum), so all ranks make the same choice.  With
+    ``ret_cols`` > 0 the workspace also holds a return region of W*El*gm_cap
+    rows of ``ret_cols`` bf16 values (the combine path).
     """
     gm_cap = 1
     while gm_cap < max(gm, 1):
         gm_cap *= 2
     cap_rows = max(W - 1, 0) * El * gm_cap
     max_chunks = (gm_cap + push_rows - 1) // push_rows
-    key = WorkspaceKey(W, El, H, cap_rows, max_chunks, push_rows, device, group_name(group))
+    ret_rows = W * El * gm_cap if ret_cols > 0 else 0
+    key = WorkspaceKey(W, El, H, cap_rows, max_chunks, push_rows, device, group_name(group), ret_rows,
+                       ret_cols if ret_cols > 0 else 0)
     ws = _CACHE.get(key)
     if ws is None:
         ws = SymmetricWorkspace(key, group, rank)

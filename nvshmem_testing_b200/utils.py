@@ -31,14 +31,18 @@ class Routing:
     offsets: torch.Tensor    # [E+1] int32: exclusive scan of counts
     perm: torch.Tensor       # [T*K] int32: first offsets[E] entries are token ids grouped by expert
     max_count: torch.Tensor  # [1] int32: local max bucket
+    slots: torch.Tensor | None = None  # [T, K] int32: row of (t, k) inside its bucket, -1 if not routed
 
 
 def _stream_ptr(dev: torch.device) -> ctypes.c_void_p:
     return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
 
 
-def route(top_idxs: torch.Tensor, num_experts: int) -> Routing:
-    """Per-expert counts, offsets and stable token permutation (no host sync)."""
+def route(top_idxs: torch.Tensor, num_experts: int, with_slots: bool = False) -> Routing:
+    """Per-expert counts, offsets and stable token permutation (no host sync).
+
+    ``with_slots`` also returns, per (token, k), the token's row inside the
+    bucket of ``top_idxs[t, k]`` (the key the combine step gathers with)."""
     if not top_idxs.is_cuda:
         raise ValueError("top_idxs must be a CUDA tensor")
     if top_idxs.dim() == 1:
@@ -52,6 +56,12 @@ def route(top_idxs: torch.Tensor, num_experts: int) -> Routing:
     offsets = torch.empty(num_experts + 1, dtype=torch.int32, device=dev)
     perm = torch.empty(max(T * K, 1), dtype=torch.int32, device=dev)
     maxc = torch.empty(1, dtype=torch.int32, device=dev)
+    if with_slots:
+        slots = torch.empty((T, K), dtype=torch.int32, device=dev)
+        N.check(N.lib().moe_route_slots(ids.data_ptr(), int(ids.dtype == torch.int64), T, K, num_experts,
+                                        counts.data_ptr(), offsets.data_ptr(), perm.data_ptr(), slots.data_ptr(),
+                                        maxc.data_ptr(), _stream_ptr(dev)), "moe_route_slots")
+        return Routing(counts, offsets, perm, maxc, slots)
     N.check(N.lib().moe_route(ids.data_ptr(), int(ids.dtype == torch.int64), T, K, num_experts, counts.data_ptr(),
                               offsets.data_ptr(), perm.data_ptr(), maxc.data_ptr(), _stream_ptr(dev)), "moe_route")
     return Routing(counts, offsets, perm, maxc)

@@ -93,3 +93,13 @@ def weights(w: Workload, rank: int, world_size: int, device="cpu") -> torch.Tens
     g = _gen(w.seed + 10086 + rank, device)
     El = w.local_experts(world_size)
     return (0.02 * torch.randn(El, w.H, w.N, generator=g, device=device, dtype=torch.float32)).to(w.dtype)
+
+
+def top_vals(w: Workload, rank: int, device="cpu") -> torch.Tensor:
+    """[T, K] float32 router weights for the combine step: a softmax over
+    seeded N(0, 1) logits of the K chosen experts (the renormalised top-k
+    weights of a softmax router); for top-1, the sigmoid of the logit."""
+    g = _gen(w.seed * 7919 + 4242 + rank, device)
+    K = 1 if (w.routing == "top1" or w.K == 1) else w.K
+    logits = torch.randn(w.T, K, generator=g, device=device, dtype=torch.float32)
+    return logits.softmax(dim=-1) if K > 1 else logits.sigmoid()

@@ -13,3 +13,4 @@ output.  ``tests/test_oracle.py`` checks this oracle against them.
 """
 from .routing import bucketize, local_max, pad_coalesce, gen_tensor_restated, recv_counts_matrix  # noqa: F401
 from .layer import alltoall_equal, baseline_run, ep_layer, bf16_bits_to_f32, f32_to_bf16_bits  # noqa: F401
+from .layer import route_slots, combine_layer, combine_from_outputs  # noqa: F401

@@ -43,3 +43,97 @@ def ep_layer(send: list[np.ndarray], chunk: int, weights: list[np.ndarray]) -> l
     W = len(send)
     recv = alltoall_equal(send, chunk)
     return [baseline_run(recv[r], chunk, W, weights[r]) for r in range(W)]
+
+
+# ---------------------------------------------------------------- return path
+# The step after the reference's path: expert outputs go back to the rank
+# that sent each token and are summed with the router's top-k weights
+# (top_vals, computed at utils.py:24-25 and unused by the reference).  The
+# selection rule is the routing's (utils.py:31): a repeated id counts once,
+# ids outside [0, E) are skipped.  The expert output is rounded to bf16 (the
+# dtype the layer stores it in) before the fp32 weighted sum.
+
+def route_slots(top_idxs: np.ndarray, num_experts: int) -> np.ndarray:
+    """[T, K] int32: the row of token t inside bucket top_idxs[t, k] (its
+    index in the ascending token list of that expert), -1 for a repeated or
+    out-of-range id."""
+    from .routing import bucketize
+    ids = np.asarray(top_idxs)
+    if ids.ndim == 1:
+        ids = ids[:, None]
+    counts, offsets, perm = bucketize(ids, num_experts)
+    T, K = ids.shape
+    slots = np.full((T, K), -1, np.int32)
+    for t in range(T):
+        seen = set()
+        for k in range(K):
+            e = int(ids[t, k])
+            if e < 0 or e >= num_experts or e in seen:
+                continue
+            seen.add(e)
+            bucket = perm[offsets[e]:offsets[e + 1]]
+            slots[t, k] = int(np.searchsorted(bucket, t))
+    return slots
+
+
+def _bf16_round(x: np.ndarray) -> np.ndarray:
+    return bf16_bits_to_f32(f32_to_bf16_bits(x))
+
+
+def combine_layer(x: list[np.ndarray], ids: list[np.ndarray], vals: list[np.ndarray],
+                  weights: list[np.ndarray]) -> list[np.ndarray]:
+    """y[r] [T_r, N] fp32 (before the final bf16 rounding) for every rank r:
+    y[t] = sum over distinct valid ids e of row t of vals[t, k] * bf16(x[t] @ W_e),
+    with expert e held by rank e // El as weights[e // El][e % El]."""
+    W = len(x)
+    El = weights[0].shape[0]
+    E = El * W
+    out = []
+    for r in range(W):
+        xr = np.asarray(x[r], np.float32)
+        idr = np.asarray(ids[r])
+        if idr.ndim == 1:
+            idr = idr[:, None]
+        vr = np.asarray(vals[r], np.float32).reshape(idr.shape)
+        T, K = idr.shape
+        y = np.zeros((T, weights[0].shape[2]), np.float32)
+        first = np.ones((T, K), bool)
+        for k in range(K):
+            for j in range(k):
+                first[:, k] &= idr[:, j] != idr[:, k]
+        for e in range(E):
+            for k in range(K):
+                sel = np.nonzero((idr[:, k] == e) & first[:, k])[0]
+                if sel.size == 0:
+                    continue
+                rows = _bf16_round(xr[sel] @ weights[e // El][e % El].astype(np.float32))
+                y[sel] += vr[sel, k][:, None] * rows
+        out.append(y)
+    return out
+
+
+def combine_from_outputs(outs: list[np.ndarray], ids: list[np.ndarray], vals: list[np.ndarray],
+                         gm: int) -> list[np.ndarray]:
+    """The same combine read from the layer's own outputs: outs[o] is rank o's
+    [El, W*gm, N] result of ``ep_layer`` (row src*gm + j of expert le is the
+    j-th token that rank src routed to expert o*El + le)."""
+    W = len(outs)
+    El = outs[0].shape[0]
+    E = El * W
+    res = []
+    for r in range(W):
+        idr = np.asarray(ids[r])
+        if idr.ndim == 1:
+            idr = idr[:, None]
+        vr = np.asarray(vals[r], np.float32).reshape(idr.shape)
+        slots = route_slots(idr, E)
+        T, K = idr.shape
+        y = np.zeros((T, outs[0].shape[2]), np.float32)
+        for t in range(T):
+            for k in range(K):
+                if slots[t, k] < 0:
+                    continue
+                e = int(idr[t, k])
+                y[t] += vr[t, k] * _bf16_round(outs[e // El][e % El, r * gm + slots[t, k]])
+        res.append(y)
+    return res

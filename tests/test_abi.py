@@ -41,6 +41,22 @@ def test_workspace_layout_is_host_only_and_aligned():
     # count matrix: two parities of [W][W][El] int32
     assert L.off_cflag - L.off_cmat >= 2 * 8 * 8 * 32 * 4
     assert L.off_free - L.off_dflag >= 2 * 8 * 32 * 8 * 4
+    # "returned" flags share the free-epoch block; no return region by default
+    assert L.off_free + 8 * 4 <= L.off_rflag and L.off_rflag + 8 * 4 <= L.off_local
+    assert L.ret_bytes == 0 and L.off_ret + L.ret_bytes <= L.total_bytes
+
+
+def test_workspace_layout_with_return_region():
+    base = N.workspace_layout(8, 32, 7168, 2, 7 * 32 * 256, 8)
+    L = N.workspace_layout(8, 32, 7168, 2, 7 * 32 * 256, 8, 8 * 32 * 256, 2048)
+    # control and receive regions are unchanged; the return region follows
+    assert (L.off_cmat, L.off_rflag, L.off_local, L.ctrl_bytes, L.off_data) == \
+        (base.off_cmat, base.off_rflag, base.off_local, base.ctrl_bytes, base.off_data)
+    assert L.off_ret % 4096 == 0 and L.off_ret >= L.off_data + 2 * 7 * 32 * 256 * 7168 * 2
+    assert L.ret_bytes == 8 * 32 * 256 * 2048 * 2 and L.total_bytes >= L.off_ret + L.ret_bytes
+    # the no-allocation entry point's one-rank control region still fits its scratch
+    one = N.workspace_layout(1, N.NOALLOC_MAX_EXPERTS, 4096, 2, 0, 1)
+    assert one.ctrl_bytes + 256 <= 2048
 
 
 def test_bad_arguments_are_rejected_before_any_device_call():
@@ -56,6 +72,14 @@ def test_bad_arguments_are_rejected_before_any_device_call():
     assert lib.moe_ep_run(ctypes.byref(p), None) == N.BAD_ARG
     bad = N.Layout()
     assert lib.moe_ep_workspace_layout(0, 1, 1, 2, 0, 1, ctypes.byref(bad)) == N.BAD_ARG
+    assert lib.moe_ep_workspace_layout_ret(1, 1, 1, 2, 0, 1, -1, 8, ctypes.byref(bad)) == N.BAD_ARG
+    assert lib.moe_route_slots(None, 0, 10, 1, 4, None, None, None, None, None, None) == N.BAD_ARG
+    c = N.CombineParams()
+    assert lib.moe_ep_run_combine(None, ctypes.byref(c), None) == N.BAD_ARG
+    c.T, c.K, c.ret_rows = 4, 2, 0  # no return region
+    assert lib.moe_ep_run_combine(ctypes.byref(p), ctypes.byref(c), None) == N.BAD_ARG
+    c.ret_rows, c.K = 64, 33  # K above the routing limit
+    assert lib.moe_ep_run_combine(ctypes.byref(p), ctypes.byref(c), None) == N.BAD_ARG
 
 
 def test_status_word_decoding():
