@@ -456,8 +456,9 @@ def main(argv=None) -> int:
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-nccl", action="store_true")
-    ap.add_argument("--path", choices=["dispatch_gemm", "combine"], default="dispatch_gemm",
-                    help="dispatch_gemm: the reference's path (default); combine: with return + top-k combine")
+    ap.add_argument("--path", choices=["dispatch_gemm", "general", "combine"], default="dispatch_gemm",
+                    help="dispatch_gemm: the reference's path (default); general: the unpadded exchange "
+                         "(general_a2a=True); combine: with return + top-k combine")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -476,10 +477,13 @@ def main(argv=None) -> int:
     ids_cpu = workloads.top_idxs(wl, rank)
     ids = ids_cpu.to(dev)
     weights = workloads.weights(wl, rank, world, device=dev)
+    general = args.path == "general"
     coalesced, chunk, lengths = utils.dispatch(tokens, ids, wl.E, world)
     counts = torch.tensor(lengths, dtype=torch.int32, device=dev)
     recv_counts = utils.recv_counts_from(counts, world)
     gm = chunk // El
+    if general:  # compact send buffer; the padded one stays for the NCCL arm
+        compact, total, _ = utils.dispatch(tokens, ids, wl.E, world, general_a2a=True)
     rc_cpu = recv_counts.cpu()
     rows_in = int(rc_cpu.sum())
     remote_in = rows_in - int(rc_cpu[rank].sum())
@@ -488,6 +492,9 @@ def main(argv=None) -> int:
     nvlink_bytes = max(remote_in, remote_out) * wl.H * 2
 
     def step():
+        if general:
+            return apg.run(rank, compact, total, 1, wl.T, wl.H, wl.E, world, None, True, weights, recv_counts,
+                           max_count=gm, recv_rows=rows_in)
         return apg.run(rank, coalesced, chunk, 1, wl.T, wl.H, wl.E, world, None, False, weights, recv_counts)
 
     # correctness guard against the NCCL path on this very input
@@ -497,6 +504,9 @@ def main(argv=None) -> int:
     ok = True
     if not args.no_nccl:
         ref = nccl_a2a_bmm(coalesced, chunk, world, weights)
+        if general:  # drop the padded rows of the NCCL result: cells (le, src) back to back
+            ref = torch.cat([ref[le, src * gm:src * gm + int(rc_cpu[src, le])]
+                             for le in range(El) for src in range(world)])
         ok = bool(torch.allclose(ours.float(), ref.float(), rtol=1e-2, atol=1e-2))
         del ref
     del ours
@@ -518,16 +528,16 @@ def main(argv=None) -> int:
     # ---- end to end through the public API from pinned host buffers
     tok_host = workloads.tokens(wl, rank).pin_memory()  # CPU-generated, same shape/distribution
     ids_host = ids_cpu.pin_memory()
-    out_host = torch.empty((El, world * gm, wl.N), dtype=torch.bfloat16).pin_memory()
+    out_host = torch.empty((rows_in, wl.N) if general else (El, world * gm, wl.N), dtype=torch.bfloat16).pin_memory()
     h2d = tok_host.numel() * tok_host.element_size() + ids_host.numel() * ids_host.element_size()
     d2h = out_host.numel() * out_host.element_size()
 
     def e2e_step():
         t = tok_host.to(dev, non_blocking=True)
         i = ids_host.to(dev, non_blocking=True)
-        co, ch, ln = utils.dispatch(t, i, wl.E, world)
+        co, ch, ln = utils.dispatch(t, i, wl.E, world, general_a2a=general)
         rc = utils.recv_counts_from(torch.tensor(ln, dtype=torch.int32, device=dev), world)
-        o = apg.run(rank, co, ch, 1, wl.T, wl.H, wl.E, world, None, False, weights, rc)
+        o = apg.run(rank, co, ch, 1, wl.T, wl.H, wl.E, world, None, general, weights, rc)
         out_host.copy_(o, non_blocking=True)
         torch.cuda.current_stream().synchronize()
 
@@ -551,7 +561,8 @@ def main(argv=None) -> int:
     # Algorithmic HBM bytes of one launch on this rank: expert weights once,
     # every valid row once, the whole padded output, and the remote rows read
     # for sending plus written by peers.
-    hbm_bytes = (El * wl.H * wl.N * 2 + rows_in * wl.H * 2 + El * world * gm * wl.N * 2
+    out_rows = rows_in if general else El * world * gm  # the compact output has no padded rows
+    hbm_bytes = (El * wl.H * wl.N * 2 + rows_in * wl.H * 2 + out_rows * wl.N * 2
                  + (remote_in + remote_out) * wl.H * 2)
     t_gemm_us = flops_rank / (peak * 1e12) * 1e6
     t_hbm_us = hbm_bytes / (hbm_peak * 1e9) * 1e6
@@ -567,7 +578,8 @@ def main(argv=None) -> int:
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_max, "us_per_layer": ms_max * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
-        "config": {"workload": wl.name, "tokens_per_rank": wl.T, "hidden": wl.H, "experts": wl.E,
+        "config": {"workload": wl.name + ("+general_a2a" if general else ""), "tokens_per_rank": wl.T,
+                   "hidden": wl.H, "experts": wl.E,
                    "local_experts": El, "top_k": wl.K, "out_dim": wl.N, "routing": wl.routing, "gm": gm,
                    "parallelism": f"ep{world}", "l2": "inputs larger than L2 (weights and tokens > 126 MB)"},
         "parity_vs_nccl_allclose": ok,

@@ -18,6 +18,10 @@
  *   moe_ep_run                  alltoall_persistent_gemm.py:207-309 (run:
  *                               peer copies + flags + fused grouped GEMM) and
  *                               baseline.py:8-56 (same output contract)
+ *   moe_pack_compact,           the general (unbalanced) all-to-all that
+ *   moe_ep_run_compact          alltoall_persistent_gemm.py:221-222 and
+ *                               baseline.py:15-16 leave as stubs: unpadded
+ *                               send buffer and output
  *   moe_route_slots,            the step after the reference's path: the
  *   moe_ep_workspace_layout_ret, return of expert outputs to their source
  *   moe_ep_run_combine          ranks and the top-k weighted sum with the
@@ -76,6 +80,13 @@ int moe_route_slots(const void* top_idxs, int ids_are_int64, int64_t T, int K, i
  * H * elem_bytes % 16 == 0 and gm >= max(counts). */
 int moe_pack_padded(const void* tokens, int64_t H, int elem_bytes, const int32_t* counts, const int32_t* offsets,
                     const int32_t* perm, int E, int64_t gm, void* out, void* stream);
+
+/* The general all-to-all's send buffer (no counterpart in the reference,
+ * whose general_a2a path is a stub): out[r, :] = tokens[perm[r], :] for
+ * r < rows, with rows = offsets[E] of moe_route, i.e. every bucket back to
+ * back in expert order without padding. */
+int moe_pack_compact(const void* tokens, int64_t H, int elem_bytes, const int32_t* perm, int64_t rows, void* out,
+                     void* stream);
 
 /* ---------------------------------------------------------------- symmetric memory
  * Replaces the torch symmetric-memory allocation + rendezvous of
@@ -167,6 +178,21 @@ typedef struct moe_ep_run_params {
 #define MOE_EP_TRACE_KBLOCKS 18       /* k-blocks issued by the MMA issuer (count)    */
 
 int moe_ep_run(const moe_ep_run_params* params, void* stream);
+
+/* The general (unbalanced) all-to-all: moe_ep_run without padding, for the
+ * general_a2a=True path that the reference leaves unimplemented
+ * (alltoall_persistent_gemm.py:221-222, baseline.py:15-16).
+ *   tokens [send_rows, H]: the cells (d, le) — rows for rank d's local expert
+ *          le — back to back in (d, le) order, recv_counts_d[rank, le] rows
+ *          each (moe_pack_compact output);
+ *   out    [out_rows, N]: the cells (le, src) back to back in (le, src)
+ *          order, recv_counts[src, le] rows each: row
+ *          sum_{(le',s') < (le,src)} recv_counts[s', le'] + i is
+ *          tokens_src[that cell's row i] @ weights[le].
+ * gm is a bound on every count (the workspace is sized by it); nothing is
+ * zero-filled.  A cell layout larger than send_rows or out_rows latches
+ * MOE_EP_BAD_ARG on the device instead of touching memory beyond them. */
+int moe_ep_run_compact(const moe_ep_run_params* params, int64_t send_rows, int64_t out_rows, void* stream);
 
 /* No counterpart in the reference.  The single-rank form of moe_ep_run for
  * callers that cannot allocate device memory: a host that reaches the library

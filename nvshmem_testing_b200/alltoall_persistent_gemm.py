@@ -52,25 +52,28 @@ def raise_if_device_error(ws) -> None:
         raise N.MoeEpError(code, "moe_ep_run (device)", f"site={site} detail={detail}; the workspace is unusable")
 
 
-def _launch_params(me: int, W: int, tokens: torch.Tensor, transmit_size: int, hidden_dim: int,
+def _launch_params(me: int, W: int, tokens: torch.Tensor, gm: int | None, transmit_size: int, hidden_dim: int,
                    local_weights: torch.Tensor, recv_counts, group, timeout_s, push_rows, num_ctas, trace,
                    ret_cols: int = 0):
     """Validate the fused layer's inputs and fill ``moe_ep_run_params``.
 
-    Returns ``(workspace, params, (El, gm, N), keepalive)``; ``ret_cols`` > 0
-    selects a workspace with a return region (the combine path)."""
+    ``gm`` is the bound on every (rank, expert) count; ``None`` means the
+    padded layout's ``transmit_size // El``.  Returns
+    ``(workspace, params, (El, gm, N), keepalive)``; ``ret_cols`` > 0 selects
+    a workspace with a return region (the combine path)."""
     if local_weights is None:
         raise ValueError("local_weights [El, H, N] is required")
     El, H, Nout = local_weights.shape
     if tokens.dim() != 2 or tokens.shape[1] != H or H != hidden_dim:
         raise ValueError(f"tokens {tuple(tokens.shape)} / hidden_dim {hidden_dim} do not match weights {tuple(local_weights.shape)}")
-    if transmit_size % El:
-        raise ValueError(f"transmit_size {transmit_size} is not a multiple of the {El} local experts")
+    if gm is None:
+        if transmit_size % El:
+            raise ValueError(f"transmit_size {transmit_size} is not a multiple of the {El} local experts")
+        gm = transmit_size // El
     if tokens.dtype != torch.bfloat16 or local_weights.dtype != torch.bfloat16:
         raise TypeError("tokens and local_weights must be bfloat16")
     if local_weights.device != tokens.device:
         raise ValueError("tokens and local_weights must be on the same device")
-    gm = transmit_size // El
     dev = tokens.device.index if tokens.device.index is not None else torch.cuda.current_device()
     tokens = tokens.contiguous()
     local_weights = local_weights.contiguous()
@@ -103,12 +106,38 @@ def _launch_params(me: int, W: int, tokens: torch.Tensor, transmit_size: int, hi
     return ws, p, (El, gm, Nout), (tokens, local_weights, recv_counts)
 
 
+def _general_bound(recv_counts: torch.Tensor, group) -> tuple[int, int]:
+    """(rows this rank receives, MAX over the group of every count): one
+    read of the W x El counts and, with more than one rank, one all-reduce."""
+    rc = recv_counts.to(torch.int64)
+    local = torch.stack([rc.sum(), rc.max() if rc.numel() else torch.zeros((), dtype=torch.int64,
+                                                                         device=rc.device)])
+    host = local.cpu()
+    m = torch.tensor([int(host[1])], dtype=torch.int64, device=recv_counts.device)
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
+        dist.all_reduce(m, op=dist.ReduceOp.MAX, group=group)
+    return int(host[0]), max(int(m.item()), 1)
+
+
 def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: int, hidden_dim: int,
         num_experts: int, world_size: int, shmem=None, general_a2a: bool = False,
         local_weights: torch.Tensor = None, recv_counts: torch.Tensor = None, *, group=None,
         timeout_s: float | None = None, push_rows: int | None = None, num_ctas: int = 0,
-        check: bool = False, trace: torch.Tensor | None = None) -> torch.Tensor:
+        check: bool = False, trace: torch.Tensor | None = None, max_count: int | None = None,
+        recv_rows: int | None = None) -> torch.Tensor:
     """Fused dispatch + grouped GEMM; see the module docstring.
+
+    ``general_a2a=True`` (a stub in the reference, alltoall_persistent_gemm.py:221-222)
+    runs the unpadded exchange: ``tokens`` is the compact send buffer
+    ``[transmit_size, H]`` of ``utils.dispatch(..., general_a2a=True)`` —
+    the cells (d, le) back to back in (d, le) order — ``recv_counts`` is
+    required, and the result is compact, ``[recv_counts.sum(), N]``: the
+    cells (le, src) back to back in (le, src) order, ``recv_counts[src, le]``
+    rows each.  Its buffers are sized by the largest count over the group
+    and the output by the rows this rank receives: pass ``max_count`` (the
+    same on every rank, at least every count) and ``recv_rows``
+    (``recv_counts.sum()``) to keep the call free of host synchronisation;
+    otherwise both are read from ``recv_counts`` (the maximum all-reduced).
 
     Keyword-only extensions: ``group`` (process group, default WORLD),
     ``timeout_s`` (bound on every device wait for a peer), ``push_rows``
@@ -117,20 +146,38 @@ def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: in
     ``trace`` (int64 device tensor of at least ``num_sms * 24`` words that
     receives the per-CTA device timeline, ``_native.TRACE_FIELDS``).
     """
-    if general_a2a:
-        raise NotImplementedError("general/unbalanced a2a not implemented.")
     assert dist.is_initialized()
     assert tokens.is_cuda
-    assert tokens.shape[0] == transmit_size * world_size
     me, W = _group_info(group, world_size, rank)
     if W != world_size or me != rank:
         raise ValueError(f"rank/world_size ({rank}/{world_size}) disagree with the process group ({me}/{W})")
-    ws, p, (El, gm, Nout), keep = _launch_params(me, W, tokens, transmit_size, hidden_dim, local_weights,
-                                                 recv_counts, group, timeout_s, push_rows, num_ctas, trace)
-    out = torch.empty((El, W * gm, Nout), dtype=torch.bfloat16, device=tokens.device)
-    p.out = out.data_ptr()
-    stream = torch.cuda.current_stream(tokens.device)
-    N.check(N.lib().moe_ep_run(ctypes.byref(p), ctypes.c_void_p(stream.cuda_stream)), "moe_ep_run")
+    if general_a2a:
+        if recv_counts is None:
+            raise ValueError("general_a2a needs recv_counts [W, El]")
+        if tokens.shape[0] != transmit_size:
+            raise ValueError(f"general_a2a: tokens has {tokens.shape[0]} rows, transmit_size is {transmit_size}")
+        if max_count is None or recv_rows is None:
+            rows_h, bound = _general_bound(recv_counts, group)
+        out_rows = int(recv_rows) if recv_rows is not None else rows_h
+        gm = max(int(max_count), 1) if max_count is not None else bound
+        send_rows = tokens.shape[0]
+        if send_rows == 0:  # nothing to send: any valid 16-byte-aligned row serves as the (unread) buffer
+            tokens = torch.zeros((1, tokens.shape[1]), dtype=tokens.dtype, device=tokens.device)
+        ws, p, (El, gm, Nout), keep = _launch_params(me, W, tokens, gm, transmit_size, hidden_dim, local_weights,
+                                                     recv_counts, group, timeout_s, push_rows, num_ctas, trace)
+        out = torch.empty((max(out_rows, 1), Nout), dtype=torch.bfloat16, device=tokens.device)[:out_rows]
+        p.out = out.data_ptr()
+        stream = torch.cuda.current_stream(tokens.device)
+        N.check(N.lib().moe_ep_run_compact(ctypes.byref(p), send_rows, out_rows,
+                                           ctypes.c_void_p(stream.cuda_stream)), "moe_ep_run_compact")
+    else:
+        assert tokens.shape[0] == transmit_size * world_size
+        ws, p, (El, gm, Nout), keep = _launch_params(me, W, tokens, None, transmit_size, hidden_dim, local_weights,
+                                                     recv_counts, group, timeout_s, push_rows, num_ctas, trace)
+        out = torch.empty((El, W * gm, Nout), dtype=torch.bfloat16, device=tokens.device)
+        p.out = out.data_ptr()
+        stream = torch.cuda.current_stream(tokens.device)
+        N.check(N.lib().moe_ep_run(ctypes.byref(p), ctypes.c_void_p(stream.cuda_stream)), "moe_ep_run")
     if check:
         stream.synchronize()
         raise_if_device_error(ws)

@@ -78,7 +78,7 @@ def run(rank: int, tokens: torch.Tensor, transmit_size: int, world_size: int, lo
     if local_weights is None or local_weights.dim() != 3:
         raise ValueError("local_weights [El, H, N] is required")
     Nout = local_weights.shape[2]
-    ws, p, (El, gm, Nout), keep = _launch_params(me, W, tokens, transmit_size, tokens.shape[1], local_weights,
+    ws, p, (El, gm, Nout), keep = _launch_params(me, W, tokens, None, transmit_size, tokens.shape[1], local_weights,
                                                  recv_counts, group, timeout_s, push_rows, num_ctas, trace,
                                                  ret_cols=Nout)
     ids, vals, sl = top_idxs.contiguous(), top_vals.contiguous(), slots.contiguous()

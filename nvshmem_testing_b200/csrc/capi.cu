@@ -66,6 +66,17 @@ int moe_pack_padded(const void* tokens, int64_t H, int elem_bytes, const int32_t
                             static_cast<cudaStream_t>(stream));
 }
 
+int moe_pack_compact(const void* tokens, int64_t H, int elem_bytes, const int32_t* perm, int64_t rows, void* out,
+                     void* stream) {
+  if (H <= 0 || elem_bytes <= 0 || (H * elem_bytes) % 16 || rows < 0 || (rows > 0 && (!tokens || !perm || !out)))
+    return kBadArg;
+  if ((reinterpret_cast<uintptr_t>(tokens) | reinterpret_cast<uintptr_t>(out)) & 15) return kBadArg;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return kCudaErr;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return kCudaErr;
+  return launch_pack_compact(tokens, H, elem_bytes, perm, rows, out, sms, static_cast<cudaStream_t>(stream));
+}
+
 int moe_symm_alloc(int device, size_t bytes, size_t* mapped_bytes, uint64_t* ptr, int* fd, uint64_t* handle) {
   if (bytes == 0 || !mapped_bytes || !ptr || !fd || !handle) return kBadArg;
   if (set_device(device) != kOk) return kCudaErr;
@@ -182,7 +193,16 @@ int moe_ep_workspace_layout_ret(int W, int El, int64_t H, int elem_bytes, int64_
 
 int moe_ep_run(const moe_ep_run_params* params, void* stream) {
   if (!params) return kBadArg;
-  return launch_fused(params, 0, static_cast<cudaStream_t>(stream));
+  return launch_fused(params, FusedMode{}, static_cast<cudaStream_t>(stream));
+}
+
+int moe_ep_run_compact(const moe_ep_run_params* params, int64_t send_rows, int64_t out_rows, void* stream) {
+  if (!params || send_rows < 0 || out_rows < 0) return kBadArg;
+  FusedMode m;
+  m.general = 1;
+  m.send_rows = send_rows;
+  m.out_rows = out_rows;
+  return launch_fused(params, m, static_cast<cudaStream_t>(stream));
 }
 
 int moe_ep_run_combine(const moe_ep_run_params* run, const moe_ep_combine_params* c, void* stream) {
@@ -197,7 +217,9 @@ int moe_ep_run_combine(const moe_ep_run_params* run, const moe_ep_combine_params
   if (workspace_layout(run->world_size, run->local_experts, run->hidden, run->elem_bytes, run->cap_rows,
                        run->max_chunks, c->ret_rows, run->out_dim, &L) != kOk)
     return kBadArg;
-  const int rc = launch_fused(run, c->ret_rows, s);
+  FusedMode m;
+  m.ret_rows = c->ret_rows;
+  const int rc = launch_fused(run, m, s);
   if (rc != kOk) return rc;
   return launch_combine(run, c, L, s);
 }

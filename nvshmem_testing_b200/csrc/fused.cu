@@ -104,6 +104,11 @@ struct Params {
   // releases off_rflag[me] at every rank.
   int ret;
   uint64_t off_ret, off_rflag;
+  // Compact mode (general all-to-all): tokens is [send_rows, H] with the
+  // cells (d, le) back to back, unpadded; out is [out_rows, N] with the
+  // cells (le, src) back to back.  Nothing is padded or zero-filled.
+  int general;
+  int64_t send_rows, out_rows;
   int32_t* status_host;
   uint64_t* trace;  // MOE_EP_TRACE_WORDS per CTA, or null
 };
@@ -134,6 +139,8 @@ struct Sched {
   int loc_nt[kMaxLocalExperts];           // local row tiles of expert le
   int rem_nt[kMaxLocalExperts];           // remote row tiles of expert le
   int tmp[kMaxCells];                     // scratch while building
+  int soff[kMaxCells + 1];                // compact mode: [d][le] first row of my cell in tokens
+  int ooff[kMaxCells + 1];                // compact mode: [le][src] first output row of the cell
 };
 
 struct Smem {
@@ -299,7 +306,7 @@ __device__ void build_schedule(const Params& p, Sched& s, Smem& sm) {
   if (tid == 0) {
     s.nfeat = nfeat;
     s.kblocks = (p.H + KB - 1) / KB;
-    s.zero_total = p.ret ? 0 : W * El;  // return mode writes no padded output
+    s.zero_total = (p.ret || p.general) ? 0 : W * El;  // no padded output in return or compact mode
   }
   // Validation: 0 <= count <= gm everywhere, chunk slots suffice.
   for (int i = tid; i < W * W * El; i += kThreads) {
@@ -324,6 +331,10 @@ __device__ void build_schedule(const Params& p, Sched& s, Smem& sm) {
     s.push_cnt[i] = sc;
     s.push_off[i] = total;
     s.tmp[i] = before;
+    if (p.general) {
+      s.soff[i] = C(d, me, le);          // scanned below (cells d-major)
+      s.ooff[le * W + d] = s.cnt[i];     // scanned below (cells le-major)
+    }
     if (d != me) s.push_pfx[le * (W - 1) + (q_me - 1)] = (sc + p.push_rows - 1) / p.push_rows;
   }
   __syncthreads();
@@ -357,10 +368,20 @@ __device__ void build_schedule(const Params& p, Sched& s, Smem& sm) {
   //    expert, matching the expert-major order of the receivers' tiles;
   //  * push_off (per destination d, warps 3..): where my rows for (d, le)
   //    land at d = d's compact base of le + the rows that precede mine.
-  if (warp == 0) warp_exclusive_scan(s.rbase, El, lane);
+  if (warp == 0) {
+    warp_exclusive_scan(s.rbase, El, lane);
+    if (p.general) {
+      warp_exclusive_scan(s.soff, W * El, lane);
+      if (lane == 0 && int64_t(s.soff[W * El]) > p.send_rows) raise_error(p, sm, kBadArg, kSiteTable, 0xFFFE);
+    }
+  }
   if (warp == 1) {
     warp_exclusive_scan(s.tile_pfx, El, lane);
     if (lane == 0) s.tiles_total = s.tile_pfx[El];
+    if (p.general) {
+      warp_exclusive_scan(s.ooff, W * El, lane);
+      if (lane == 0 && int64_t(s.ooff[W * El]) > p.out_rows) raise_error(p, sm, kBadArg, kSiteTable, 0xFFFF);
+    }
   }
   if (warp == 2) {
     warp_exclusive_scan(s.push_pfx, El * (W - 1), lane);
@@ -384,12 +405,16 @@ __device__ void build_schedule(const Params& p, Sched& s, Smem& sm) {
 
 __device__ __forceinline__ int64_t out_row_of(const Sched& s, const Params& p, const Tile& tl, int row) {
   const int W = p.W;
-  if (!tl.remote) return (int64_t(tl.le) * W + p.me) * p.gm + row;
-  const int* sg = s.seg + tl.le * (W + 1);
-  int q = 1;
-  while (q < W - 1 && row >= sg[q + 1]) ++q;
-  const int src = (p.me + q) % W;
-  return (int64_t(tl.le) * W + src) * p.gm + (row - sg[q]);
+  int src = p.me, i = row;
+  if (tl.remote) {
+    const int* sg = s.seg + tl.le * (W + 1);
+    int q = 1;
+    while (q < W - 1 && row >= sg[q + 1]) ++q;
+    src = (p.me + q) % W;
+    i = row - sg[q];
+  }
+  if (p.general) return int64_t(s.ooff[tl.le * W + src]) + i;
+  return (int64_t(tl.le) * W + src) * p.gm + i;
 }
 
 // Return mode: where output row `row` of tile tl goes — the source rank's
@@ -541,8 +566,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (tl.remote) fence_proxy_async_global();
         const int half = tl.n >> 1;
+        const int64_t local_cell = p.general ? int64_t(s.soff[me * El + tl.le]) : (int64_t(me) * El + tl.le) * p.gm;
         const int64_t row_base = tl.remote ? int64_t(par) * p.cap_rows + s.rbase[tl.le] + tl.row0 + crank * half
-                                           : (int64_t(me) * El + tl.le) * p.gm + tl.row0 + crank * half;
+                                           : local_cell + tl.row0 + crank * half;
         const RowMaps& rm = tl.remote ? rows_remote : rows_local;
         // Feature boxes of 64 that exist (trailing features beyond N are not loaded).
         const int f_mine = tl.feat * kFeatPair + int(crank) * kFeatCta;
@@ -715,7 +741,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int j0 = chunk * p.push_rows;
         const int j1 = min(j0 + p.push_rows, s.push_cnt[d * El + le]);
         unsigned char* peer = reinterpret_cast<unsigned char*>(p.peers[d]);
-        const uint4* src = reinterpret_cast<const uint4*>(p.tokens + ((int64_t(d) * El + le) * p.gm + j0) * p.H);
+        const int64_t cell = p.general ? int64_t(s.soff[d * El + le]) : (int64_t(d) * El + le) * p.gm;
+        const uint4* src = reinterpret_cast<const uint4*>(p.tokens + (cell + j0) * p.H);
         uint4* dst = reinterpret_cast<uint4*>(peer + p.off_data +
                                               (size_t(par) * p.cap_rows + s.push_off[d * El + le] + j0) * row_bytes);
         const int64_t nvec = int64_t(j1 - j0) * int64_t(row_bytes / 16);
@@ -916,15 +943,21 @@ struct DeviceLaunchInfo {
 };
 static DeviceLaunchInfo g_launch_info[kMaxDevices];
 
+// The whole shared-memory plan must fit the 227 KB a CTA may opt in to.
+static_assert(1024 + size_t(kStages) * kStageBytes + kEpiStageBytes + sizeof(Sched) + sizeof(Smem) <= 227 * 1024,
+              "shared memory plan exceeds 227 KB");
+
 size_t fused_smem_bytes() {
   return 1024 + size_t(kStages) * kStageBytes + kEpiStageBytes + sizeof(Sched) + sizeof(Smem);
 }
 
-// ret_rows > 0 selects return mode: output rows go to the source ranks'
+// m.ret_rows > 0 selects return mode: output rows go to the source ranks'
 // return regions (ret_rows rows of out_dim bf16 each, at least W*El*gm) and
-// `out` is not used.
-int launch_fused(const moe_ep_run_params* a, int64_t ret_rows, cudaStream_t stream) {
+// `out` is not used.  m.general selects compact mode (send_rows rows of
+// tokens, out_rows rows of out, no padding).
+int launch_fused(const moe_ep_run_params* a, const FusedMode& m, cudaStream_t stream) {
   const int W = a->world_size, El = a->local_experts;
+  const int64_t ret_rows = m.ret_rows;
   if (W < 1 || W > 64 || a->rank < 0 || a->rank >= W || El < 1 || El > kMaxLocalExperts || W * El > kMaxCells)
     return kBadArg;
   if (a->elem_bytes != 2 || a->hidden <= 0 || a->out_dim <= 0 || a->hidden % 8 || a->out_dim % 8 || a->gm < 0)
@@ -934,12 +967,15 @@ int launch_fused(const moe_ep_run_params* a, int64_t ret_rows, cudaStream_t stre
   if (!a->tokens || !a->weights || (!ret && !a->out) || !a->peer_bases || !a->local_base || !a->recv_counts)
     return kBadArg;
   if (ret && ret_rows < int64_t(W) * El * a->gm) return kBadArg;
+  if (m.general && (ret || m.send_rows < 0 || m.out_rows < 0)) return kBadArg;
   if ((reinterpret_cast<uintptr_t>(a->tokens) | reinterpret_cast<uintptr_t>(a->weights) |
        reinterpret_cast<uintptr_t>(a->out)) & 15)
     return kBadArg;
   if (a->num_ctas & 1u) return kBadArg;  // CTA pairs
-  const int64_t rows_in = int64_t(W) * El * a->gm;
-  if (rows_in + kMaxTileRows > (int64_t(1) << 31) || 2 * a->cap_rows + kMaxTileRows > (int64_t(1) << 31))
+  // Rows of the token buffer (the local TMA map's extent).
+  const int64_t rows_in = m.general ? m.send_rows : int64_t(W) * El * a->gm;
+  if (rows_in + kMaxTileRows > (int64_t(1) << 31) || 2 * a->cap_rows + kMaxTileRows > (int64_t(1) << 31) ||
+      m.out_rows + kMaxTileRows > (int64_t(1) << 31))
     return kBadArg;
   if (!driver().ok) return kCudaErr;
 
@@ -993,6 +1029,9 @@ int launch_fused(const moe_ep_run_params* a, int64_t ret_rows, cudaStream_t stre
   p.ret = ret;
   p.off_ret = L.off_ret;
   p.off_rflag = L.off_rflag;
+  p.general = m.general;
+  p.send_rows = m.send_rows;
+  p.out_rows = m.out_rows;
   p.status_host = a->status_host;
   p.trace = a->trace;
 

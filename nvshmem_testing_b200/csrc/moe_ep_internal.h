@@ -47,6 +47,8 @@ struct LocalWords {
   uint32_t pad;
 };
 
+int launch_pack_compact(const void* tokens, int64_t H, int elem_bytes, const int32_t* perm, int64_t rows, void* out,
+                        int num_sms, cudaStream_t stream);
 int launch_pack_padded(const void* tokens, int64_t H, int elem_bytes, const int32_t* counts, const int32_t* offsets,
                        const int32_t* perm, int E, int64_t gm, void* out, int num_sms, cudaStream_t stream);
 
@@ -73,7 +75,13 @@ const Driver& driver();
 // ---- fused dispatch + grouped GEMM (fused.cu)
 int workspace_layout(int W, int El, int64_t H, int elem_bytes, int64_t cap_rows, int max_chunks, int64_t ret_rows,
                      int64_t ret_cols, moe_ep_layout* L);
-int launch_fused(const moe_ep_run_params* a, int64_t ret_rows, cudaStream_t stream);
+struct FusedMode {
+  int64_t ret_rows = 0;   // > 0: return mode (combine path)
+  int general = 0;        // compact (unpadded) send buffer and output
+  int64_t send_rows = 0;  // compact mode: rows of tokens
+  int64_t out_rows = 0;   // compact mode: rows of out
+};
+int launch_fused(const moe_ep_run_params* a, const FusedMode& m, cudaStream_t stream);
 
 // ---- return path: top-k weighted combine (combine.cu)
 int launch_combine(const moe_ep_run_params* run, const moe_ep_combine_params* c, const moe_ep_layout& L,

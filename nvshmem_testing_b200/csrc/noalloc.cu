@@ -89,5 +89,5 @@ extern "C" int moe_ep_run_noalloc(const moe_ep_run_params* params, void* stream)
   q.push_rows = push_rows;
   q.max_chunks = 1;
   q.epoch = 1;
-  return launch_fused(&q, 0, s);
+  return launch_fused(&q, FusedMode{}, s);
 }

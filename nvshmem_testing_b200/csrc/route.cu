@@ -196,6 +196,19 @@ __global__ void pack_padded_kernel(const uint4* __restrict__ tokens, int64_t row
   }
 }
 
+// Compact expert-major pack (the general all-to-all's send buffer):
+// out[r] = tokens[perm[r]] for r < rows (rows = offsets[E]).  One warp per row.
+__global__ void pack_compact_kernel(const uint4* __restrict__ tokens, int64_t row_vecs,
+                                    const int32_t* __restrict__ perm, int64_t rows, uint4* __restrict__ out) {
+  const int64_t warps_total = int64_t(gridDim.x) * (blockDim.x >> 5);
+  const int lane = threadIdx.x & 31;
+  for (int64_t r = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps_total) {
+    const uint4* src = tokens + int64_t(perm[r]) * row_vecs;
+    uint4* dst = out + r * row_vecs;
+    for (int64_t v = lane; v < row_vecs; v += 32) dst[v] = ld_nc_v4(src + v);
+  }
+}
+
 size_t route_smem_bytes(int E) { return size_t(E) * (4 + 4 + 4 * kRouteWords + 2 * kRouteWords); }
 
 int launch_route(const void* ids, int ids_are_int64, int64_t T, int K, int E, int32_t* counts, int32_t* offsets,
@@ -227,6 +240,19 @@ int launch_pack_padded(const void* tokens, int64_t H, int elem_bytes, const int3
   if (blocks > cap) blocks = cap;
   pack_padded_kernel<<<int(blocks), threads, 0, stream>>>(static_cast<const uint4*>(tokens), row_vecs, counts,
                                                           offsets, perm, E, gm, static_cast<uint4*>(out));
+  return cudaGetLastError() == cudaSuccess ? kOk : kCudaErr;
+}
+
+int launch_pack_compact(const void* tokens, int64_t H, int elem_bytes, const int32_t* perm, int64_t rows, void* out,
+                        int num_sms, cudaStream_t stream) {
+  if (rows == 0) return kOk;
+  const int64_t row_vecs = H * elem_bytes / 16;
+  const int threads = 256;
+  int64_t blocks = (rows + (threads / 32) - 1) / (threads / 32);
+  const int64_t cap = int64_t(num_sms) * 8;
+  if (blocks > cap) blocks = cap;
+  pack_compact_kernel<<<int(blocks), threads, 0, stream>>>(static_cast<const uint4*>(tokens), row_vecs, perm, rows,
+                                                           static_cast<uint4*>(out));
   return cudaGetLastError() == cudaSuccess ? kOk : kCudaErr;
 }
 

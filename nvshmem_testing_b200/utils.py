@@ -79,6 +79,19 @@ def pack_padded(tokens: torch.Tensor, r: Routing, gm: int) -> torch.Tensor:
     return out
 
 
+def pack_compact(tokens: torch.Tensor, r: Routing, rows: int | None = None) -> torch.Tensor:
+    """``[offsets[E], H]``: every bucket back to back in expert order, no
+    padding (the general all-to-all's send buffer).  ``rows`` = offsets[E]
+    if known (otherwise read from the device)."""
+    tokens = tokens.contiguous()
+    n = int(r.offsets[-1].item()) if rows is None else int(rows)
+    H = tokens.shape[1]
+    out = torch.empty((n, H), dtype=tokens.dtype, device=tokens.device)
+    N.check(N.lib().moe_pack_compact(tokens.data_ptr(), H, tokens.element_size(), r.perm.data_ptr(), n,
+                                     out.data_ptr(), _stream_ptr(tokens.device)), "moe_pack_compact")
+    return out
+
+
 def global_max_count(r: Routing, group=None) -> int:
     """All-reduced (MAX) largest bucket; at least 1 like the reference, whose
     empty buckets carry a one-row placeholder (utils.py:36-41)."""
@@ -89,14 +102,21 @@ def global_max_count(r: Routing, group=None) -> int:
 
 
 def dispatch(tokens: torch.Tensor, top_idxs: torch.Tensor, num_experts: int, world_size: int, group=None,
-             gm: int | None = None) -> tuple[torch.Tensor, int, list[int]]:
+             gm: int | None = None, general_a2a: bool = False) -> tuple[torch.Tensor, int, list[int]]:
     """Device restatement of utils.py:28-75 for given routing ids.
 
     Returns ``(coalesced [E*gm, H], chunk_size, lengths)`` with the
     reference's conventions; ``gm`` (if given) overrides the all-reduced max.
+    With ``general_a2a`` the send buffer is compact instead — ``[sum(lengths),
+    H]``, buckets back to back in expert order — and the second value is its
+    row count (the input of ``run(..., general_a2a=True)``).
     """
     assert num_experts % world_size == 0, "Incorrect EP_SIZE, world_size should evenly divide num_experts."
     r = route(top_idxs, num_experts)
+    if general_a2a:
+        lengths = r.counts.tolist()
+        total = sum(lengths)
+        return pack_compact(tokens, r, total), total, lengths
     g = global_max_count(r, group) if gm is None else int(gm)
     coalesced = pack_padded(tokens, r, g)
     return coalesced, g * (num_experts // world_size), r.counts.tolist()

@@ -137,3 +137,36 @@ def combine_from_outputs(outs: list[np.ndarray], ids: list[np.ndarray], vals: li
                 y[t] += vr[t, k] * _bf16_round(outs[e // El][e % El, r * gm + slots[t, k]])
         res.append(y)
     return res
+
+
+# ---------------------------------------------------------------- general (unpadded) all-to-all
+
+def compact_layer(send: list[np.ndarray], all_counts: list[np.ndarray], weights: list[np.ndarray]) -> list[np.ndarray]:
+    """The layer on compact buffers.  send[r] is rank r's compact send buffer
+    (cells (d, le) back to back in (d, le) order, all_counts[r][d*El + le]
+    rows each); the result for rank r is [sum of its received rows, N] with
+    the cells (le, src) back to back in (le, src) order: cell (le, src) is
+    send[src]'s cell (r, le) @ weights[r][le], in fp32."""
+    W = len(send)
+    El = weights[0].shape[0]
+    starts = [np.concatenate([[0], np.cumsum(np.asarray(c, np.int64))]) for c in all_counts]
+    outs = []
+    for r in range(W):
+        parts = []
+        for le in range(El):
+            w = weights[r][le].astype(np.float32)
+            for src in range(W):
+                cell = r * El + le
+                rows = send[src][starts[src][cell]:starts[src][cell + 1]].astype(np.float32)
+                parts.append(rows @ w)
+        outs.append(np.concatenate(parts) if parts else np.zeros((0, weights[r].shape[2]), np.float32))
+    return outs
+
+
+def compact_from_padded(out: np.ndarray, recv_counts: np.ndarray) -> np.ndarray:
+    """[El, W*gm, N] padded layer output -> compact [(le, src) cells, N]."""
+    El, rows, N = out.shape
+    W = recv_counts.shape[0]
+    gm = rows // W
+    return np.concatenate([out[le, src * gm:src * gm + int(recv_counts[src, le])]
+                           for le in range(El) for src in range(W)])

@@ -68,3 +68,20 @@ def recv_counts_matrix(all_counts: list[np.ndarray], rank: int, world_size: int)
     El = E // world_size
     return np.stack([np.asarray(all_counts[j], np.int32)[rank * El:(rank + 1) * El]
                      for j in range(world_size)]).astype(np.int32)
+
+
+# ---------------------------------------------------------------- general (unpadded) all-to-all
+# The reference leaves general_a2a unimplemented (alltoall_persistent_gemm.py:221-222,
+# baseline.py:15-16); the unpadded layout restated here is the padded one of
+# utils.py:54-69 with the zero rows removed.
+
+def compact_coalesce(tokens: np.ndarray, counts: np.ndarray, offsets: np.ndarray, perm: np.ndarray) -> np.ndarray:
+    """Every bucket back to back in expert order, no padding:
+    rows [offsets[e], offsets[e] + counts[e]) hold bucket e."""
+    n = int(offsets[-1]) if len(offsets) else 0
+    return tokens[perm[:n]]
+
+
+def uncompact_padded(padded: np.ndarray, counts: np.ndarray, gm: int) -> np.ndarray:
+    """The compact form of a padded expert-major buffer (drop rows >= counts[e])."""
+    return np.concatenate([padded[e * gm:e * gm + int(c)] for e, c in enumerate(counts)]) if len(counts) else padded[:0]

@@ -92,7 +92,26 @@ def test_baseline_entry_point_treats_all_rows_valid(single_rank_group):
     assert bl.run(0, tok.cuda(), El * gm, 1, El * gm, H, El, 1, True, None, w.cuda()) is None
 
 
-def test_run_rejects_general_a2a(single_rank_group):
-    with pytest.raises(NotImplementedError):
+@pytest.mark.parametrize("El,H,N,gm,counts", CASES + [(3, 64, 128, 8, [0, 0, 0])])
+def test_general_a2a_single_rank_matches_oracle(single_rank_group, El, H, N, gm, counts):
+    """general_a2a=True: compact send buffer in, compact [(le, src) cells]
+    out, no padding anywhere."""
+    g = torch.Generator().manual_seed(El * 77 + H)
+    total = sum(counts)
+    tok = torch.randn(total, H, generator=g).to(torch.bfloat16)
+    w = (0.02 * torch.randn(El, H, N, generator=g)).to(torch.bfloat16)
+    rc = torch.tensor([counts], dtype=torch.int32)
+    out = apg.run(0, tok.cuda(), total, 1, total, H, El, 1, None, True, w.cuda(), rc.cuda(), check=True)
+    assert out.shape == (total, N) and out.dtype == torch.bfloat16
+    ref = oracle.compact_layer([oracle.bf16_bits_to_f32(_bits(tok))], [np.array(counts)],
+                               [oracle.bf16_bits_to_f32(_bits(w))])[0]
+    if total:
+        o = out.float().cpu().numpy()
+        np.testing.assert_allclose(o, ref, rtol=RTOL, atol=ATOL)
+        assert float(np.abs(o - ref).max()) <= MAX_REL * max(float(np.abs(ref).max()), 1e-6)
+
+
+def test_general_a2a_requires_counts(single_rank_group):
+    with pytest.raises(ValueError):
         apg.run(0, torch.zeros(2, 8, device="cuda", dtype=torch.bfloat16), 2, 1, 2, 8, 1, 1, None, True,
                 torch.zeros(1, 8, 8, device="cuda", dtype=torch.bfloat16))

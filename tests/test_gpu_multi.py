@@ -79,6 +79,17 @@ def _worker(rank, world, port, cases, q):
                 zeros = not o_[~valid].any()
                 if not (good and rel <= 1e-2 and zeros):
                     errs.append(f"call {k}: allclose={good} rel={rel:.3e} zero_padding={zeros}")
+            # the same layer through the unpadded (general) exchange
+            coal_c, total, lengths_c = utils.dispatch(tok.cuda(), ids.cuda(), wl.E, world, general_a2a=True)
+            assert lengths_c == lengths and total == sum(lengths)
+            ref_c = oracle.compact_from_padded(ref, rcm)
+            for k in range(2):
+                oc = apg.run(rank, coal_c, total, 1, wl.T, wl.H, wl.E, world, None, True, w.cuda(), rc,
+                             timeout_s=10.0).float().cpu().numpy()
+                if oc.shape != ref_c.shape or not np.allclose(oc, ref_c, rtol=RTOL, atol=ATOL):
+                    errs.append(f"general call {k}: shape {oc.shape} vs {ref_c.shape}, allclose failed")
+            torch.cuda.synchronize()
+            status |= max(wsx.host_status() for wsx in symm._CACHE.values())
             results.append((name, status, errs))
         dist.barrier()
         symm.release_all()
