@@ -165,8 +165,10 @@ def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: in
             tokens = torch.zeros((1, tokens.shape[1]), dtype=tokens.dtype, device=tokens.device)
         ws, p, (El, gm, Nout), keep = _launch_params(me, W, tokens, gm, transmit_size, hidden_dim, local_weights,
                                                      recv_counts, group, timeout_s, push_rows, num_ctas, trace)
-        out = torch.empty((max(out_rows, 1), Nout), dtype=torch.bfloat16, device=tokens.device)[:out_rows]
-        p.out = out.data_ptr()
+        # A zero-row view has a null data_ptr; the kernel wants a real buffer.
+        buf = torch.empty((max(out_rows, 1), Nout), dtype=torch.bfloat16, device=tokens.device)
+        out = buf[:out_rows]
+        p.out = buf.data_ptr()
         stream = torch.cuda.current_stream(tokens.device)
         N.check(N.lib().moe_ep_run_compact(ctypes.byref(p), send_rows, out_rows,
                                            ctypes.c_void_p(stream.cuda_stream)), "moe_ep_run_compact")
