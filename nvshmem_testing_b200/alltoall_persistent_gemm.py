@@ -16,6 +16,10 @@ Output row ``src*gm + i`` of expert ``le`` is ``recv_tokens @ W[le]`` for
 ``i < recv_counts[src, le]`` and exactly zero otherwise
 (alltoall_persistent_gemm.py:257-258, 273-291).
 
+``general_a2a=True`` (a stub in the reference, :221-222) runs the
+unpadded exchange instead: compact send buffer in, compact output out
+(``moe_ep_run_compact``; see ``run``).
+
 The work runs in one launch of the sm_100a kernel ``moe_ep_run``
 (libmoe_ep.so): counts are exchanged through the symmetric workspace, only
 valid rows cross NVLink, and each GEMM tile starts when its rows have
