@@ -310,6 +310,58 @@ def run_reference_arm(args) -> int:
     return 0
 
 
+def run_router_path(args) -> int:
+    """The router (``utils.router``: tcgen05 logits GEMM + softmax/top-k
+    kernel) on one rank's tokens, against torch's einsum + softmax + topk
+    (the reference's utils.py:23-25) on the same resident inputs."""
+    rank, world, local = init_dist(args.gpus)
+    dev = torch.device("cuda", local)
+    wl = workloads.get(args.workload, dtype=torch.bfloat16, **overrides(args))
+    x = workloads.tokens(wl, rank, device=dev)
+    g = torch.Generator(device=dev).manual_seed(wl.seed + 77)
+    rw = (0.001 * torch.randn(wl.H, wl.E, generator=g, device=dev)).to(torch.bfloat16)  # the reference's scale
+    logits = torch.empty((wl.T, wl.E), dtype=torch.bfloat16, device=dev)
+    K = wl.K
+
+    def ours():
+        return utils.router(x, rw, K, logits=logits)
+
+    def torch_router():
+        probs = torch.softmax(torch.einsum("bh,he->be", x, rw), dim=-1)
+        return torch.topk(probs, K)
+
+    v, i = ours()
+    tv, _ = torch_router()
+    torch.cuda.synchronize()
+    vals_equal = bool(torch.allclose(v, tv.float(), rtol=2 ** -7, atol=0))  # top values, tie-invariant
+    ms, clocks = time_device(ours, args.steps, args.warmup, sampler_device=local)
+    ms_t, _ = time_device(torch_router, args.steps, args.warmup)
+    ms, ms_t = max_over_ranks(ms), max_over_ranks(ms_t)
+    peaks, src = load_peaks()
+    flops = 2.0 * wl.T * wl.H * wl.E
+    hbm = wl.T * wl.H * 2 + wl.H * wl.E * 2 + 2 * wl.T * wl.E * 2 + wl.T * K * 12
+    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    hbm_peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    t_roof = max(flops / (peak * 1e12), hbm / (hbm_peak * 1e9))
+    line = {"metric": "router µs (einsum + softmax + top-k) per rank", "path": "router",
+            "value": ms * 1e3, "unit": "us", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded; router 0.001*N(0,1) like the reference)",
+            "config": {"workload": wl.name + "+router", "tokens_per_rank": wl.T, "hidden": wl.H, "experts": wl.E,
+                       "top_k": K},
+            "top_vals_match_torch": vals_equal, "torch_us": ms_t * 1e3,
+            "roofline": {"bound": "hbm" if hbm / (hbm_peak * 1e9) > flops / (peak * 1e12) else "tensor",
+                         "roofline_us": t_roof * 1e6, "frac": t_roof / (ms * 1e-3), "peak_source": src,
+                         "flops": flops, "algorithmic_hbm_bytes": hbm},
+            "gpu_launches": 3 * args.steps,  # count word, logits GEMM, softmax/top-k
+            "clocks": clocks}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0
+
+
 def run_combine_path(args) -> int:
     """The layer with its return path (``combine.run``): one JSON line like
     the default path's, with the NCCL a2a + bmm + reverse a2a + combine arm."""
@@ -456,9 +508,10 @@ def main(argv=None) -> int:
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-nccl", action="store_true")
-    ap.add_argument("--path", choices=["dispatch_gemm", "general", "combine"], default="dispatch_gemm",
+    ap.add_argument("--path", choices=["dispatch_gemm", "general", "combine", "router"], default="dispatch_gemm",
                     help="dispatch_gemm: the reference's path (default); general: the unpadded exchange "
-                         "(general_a2a=True); combine: with return + top-k combine")
+                         "(general_a2a=True); combine: with return + top-k combine; router: the router "
+                         "(einsum, softmax, top-k) before the path")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -466,6 +519,8 @@ def main(argv=None) -> int:
         return run_reference_arm(args)
     if args.path == "combine":
         return run_combine_path(args)
+    if args.path == "router":
+        return run_router_path(args)
 
     rank, world, local = init_dist(args.gpus)
     dev = torch.device("cuda", local)

@@ -18,6 +18,8 @@
  *   moe_ep_run                  alltoall_persistent_gemm.py:207-309 (run:
  *                               peer copies + flags + fused grouped GEMM) and
  *                               baseline.py:8-56 (same output contract)
+ *   moe_router                  utils.py:17-25 (router logits einsum, softmax,
+ *                               top-k: the step before the reference's path)
  *   moe_pack_compact,           the general (unbalanced) all-to-all that
  *   moe_ep_run_compact          alltoall_persistent_gemm.py:221-222 and
  *                               baseline.py:15-16 leave as stubs: unpadded
@@ -66,6 +68,23 @@ int moe_ep_num_sms(int device, int* out);
  * E <= 1024, K <= 32.  One CTA; suited to T up to ~10^5 tokens. */
 int moe_route(const void* top_idxs, int ids_are_int64, int64_t T, int K, int E, int32_t* counts, int32_t* offsets,
               int32_t* perm, int32_t* max_count, void* stream);
+
+/* Replaces the router of utils.py:17-25 (the step before the path):
+ *   logits [T, E] bf16 = x [T, H] @ router_w [H, E]   (bf16 in, fp32
+ *                        accumulation rounded once: the tcgen05 GEMM of
+ *                        moe_ep_run as a one-rank, one-expert layer)
+ *   probs              = softmax over E in fp32, rounded to bf16
+ *   top_idxs [T, K]    = the K most probable experts, descending, equal
+ *                        probabilities by ascending id (int64 or int32)
+ *   top_vals [T, K]    = their probabilities (bf16 values as float32)
+ * `logits` is caller-provided scratch (16-byte aligned).  Requires H % 8 == 0,
+ * 8 <= E <= 1024 with E % 8 == 0, 1 <= K <= min(E, 32).  The GEMM's control
+ * words live in a fixed 2 KB array inside the library, so the call allocates
+ * nothing; every call reuses that array, so router calls must not overlap
+ * each other on the GPU, and the first call on a device looks the array up
+ * synchronously (make it before any stream capture). */
+int moe_router(const void* x, int64_t T, int32_t H, const void* router_w, int32_t E, int32_t K, void* logits,
+               void* top_idxs, int32_t ids_are_int64, float* top_vals, void* stream);
 
 /* moe_route plus, for the return path,
  *   slots     [T, K] int32: j such that perm[offsets[e] + j] = t for

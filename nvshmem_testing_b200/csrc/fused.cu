@@ -109,6 +109,7 @@ struct Params {
   // cells (le, src) back to back.  Nothing is padded or zero-filled.
   int general;
   int64_t send_rows, out_rows;
+  int tile_cap;  // most rows per tile (multiple of 16, <= kMaxTileRows)
   int32_t* status_host;
   uint64_t* trace;  // MOE_EP_TRACE_WORDS per CTA, or null
 };
@@ -263,11 +264,11 @@ __device__ __forceinline__ Tile decode_tile(const Sched& s, int W, int El, int m
   return tl;
 }
 
-// Rows per tile for `rows` rows: the fewest tiles of at most 256 rows,
-// balanced, rounded up to a multiple of 16.
-__device__ __forceinline__ int tile_rows(int rows) {
+// Rows per tile for `rows` rows: the fewest tiles of at most `cap` rows
+// (a multiple of 16, at most 256), balanced, rounded up to a multiple of 16.
+__device__ __forceinline__ int tile_rows(int rows, int cap) {
   if (rows <= 0) return 16;
-  const int nt = (rows + kMaxTileRows - 1) / kMaxTileRows;
+  const int nt = (rows + cap - 1) / cap;
   return ((rows + nt - 1) / nt + 15) & ~15;
 }
 
@@ -350,8 +351,8 @@ __device__ void build_schedule(const Params& p, Sched& s, Smem& sm) {
     }
     sg[W] = run;
     const int lr = s.cnt[me * El + le];
-    s.loc_tr[le] = tile_rows(lr);
-    s.rem_tr[le] = tile_rows(run);
+    s.loc_tr[le] = tile_rows(lr, p.tile_cap);
+    s.rem_tr[le] = tile_rows(run, p.tile_cap);
     s.loc_nt[le] = (lr + s.loc_tr[le] - 1) / s.loc_tr[le];
     s.rem_nt[le] = (run + s.rem_tr[le] - 1) / s.rem_tr[le];
     s.rbase[le] = run;                                   // scanned below
@@ -968,6 +969,7 @@ int launch_fused(const moe_ep_run_params* a, const FusedMode& m, cudaStream_t st
     return kBadArg;
   if (ret && ret_rows < int64_t(W) * El * a->gm) return kBadArg;
   if (m.general && (ret || m.send_rows < 0 || m.out_rows < 0)) return kBadArg;
+  if (m.tile_cap < 0 || m.tile_cap > kMaxTileRows || m.tile_cap % 16) return kBadArg;
   if ((reinterpret_cast<uintptr_t>(a->tokens) | reinterpret_cast<uintptr_t>(a->weights) |
        reinterpret_cast<uintptr_t>(a->out)) & 15)
     return kBadArg;
@@ -1030,6 +1032,7 @@ int launch_fused(const moe_ep_run_params* a, const FusedMode& m, cudaStream_t st
   p.off_ret = L.off_ret;
   p.off_rflag = L.off_rflag;
   p.general = m.general;
+  p.tile_cap = m.tile_cap > 0 ? m.tile_cap : kMaxTileRows;
   p.send_rows = m.send_rows;
   p.out_rows = m.out_rows;
   p.status_host = a->status_host;

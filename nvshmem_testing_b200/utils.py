@@ -133,6 +133,36 @@ def recv_counts_from(counts: torch.Tensor, world_size: int, group=None) -> torch
     return recv
 
 
+def router(x: torch.Tensor, router_w: torch.Tensor, topk: int, ids_dtype=torch.int64,
+           logits: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """The router of utils.py:17-25 on the device (``moe_router``):
+    ``softmax(einsum('bh,he->be', x, router_w))`` and its top-k.
+
+    x [T, H] and router_w [H, E] bf16.  Returns ``(top_vals [T, K] float32,
+    top_idxs [T, K])``, probabilities descending (bf16 values), equal ones by
+    ascending expert id.  ``logits`` optionally supplies the [T, E] bf16
+    scratch."""
+    if x.dtype != torch.bfloat16 or router_w.dtype != torch.bfloat16:
+        raise TypeError("x and router_w must be bfloat16")
+    if not x.is_cuda or router_w.device != x.device:
+        raise ValueError("x and router_w must be CUDA tensors on one device")
+    if ids_dtype not in (torch.int32, torch.int64):
+        raise TypeError("ids_dtype must be int32 or int64")
+    x = x.contiguous()
+    router_w = router_w.contiguous()
+    T, H = x.shape
+    E = router_w.shape[1]
+    if router_w.shape[0] != H:
+        raise ValueError(f"router_w {tuple(router_w.shape)} does not match x {tuple(x.shape)}")
+    if logits is None:
+        logits = torch.empty((max(T, 1), E), dtype=torch.bfloat16, device=x.device)
+    vals = torch.empty((max(T, 1), topk), dtype=torch.float32, device=x.device)
+    ids = torch.empty((max(T, 1), topk), dtype=ids_dtype, device=x.device)
+    N.check(N.lib().moe_router(x.data_ptr(), T, H, router_w.data_ptr(), E, topk, logits.data_ptr(), ids.data_ptr(),
+                               int(ids_dtype == torch.int64), vals.data_ptr(), _stream_ptr(x.device)), "moe_router")
+    return vals[:T], ids[:T]
+
+
 def gen_weights(num_experts: int, hidden_dim: int, out_dim: int, dtype=torch.bfloat16, device="cuda"):
     """``[E, H, out]`` standard-normal expert weights (utils.py:78-80)."""
     return torch.randn(num_experts, hidden_dim, out_dim, dtype=dtype, device=device)
@@ -140,14 +170,17 @@ def gen_weights(num_experts: int, hidden_dim: int, out_dim: int, dtype=torch.bfl
 
 def gen_tensor(batch: int, seq: int, hidden_dim: int, world_size: int, num_experts: int, rank: int, topk: int,
                group=None):
-    """The reference's synthetic router (utils.py:12-25) followed by the
-    device dispatch.  The router itself (einsum, softmax, top-k) is plain
-    torch and not part of the accelerated path."""
+    """The reference's synthetic inputs (utils.py:12-22), its router
+    (utils.py:23-25: einsum, softmax, top-k) on the device through
+    ``router`` where E and H are multiples of 8 (torch otherwise), and the
+    device dispatch."""
     torch.manual_seed(rank)
     assert num_experts % world_size == 0, "Incorrect EP_SIZE, world_size should evenly divide num_experts."
     tokens = torch.rand(batch * seq, hidden_dim, dtype=torch.bfloat16).to("cuda")
-    router = torch.zeros(hidden_dim, num_experts, dtype=torch.bfloat16).to("cuda")
-    router = router + torch.randn_like(router) * 0.001
-    routed = F.softmax(torch.einsum("bh, he -> be", tokens, router), dim=-1)
-    _, top_idxs = torch.topk(routed, topk)
+    rw = torch.zeros(hidden_dim, num_experts, dtype=torch.bfloat16).to("cuda")
+    rw = rw + torch.randn_like(rw) * 0.001
+    if num_experts % 8 == 0 and hidden_dim % 8 == 0:
+        _, top_idxs = router(tokens, rw, topk)
+    else:
+        _, top_idxs = torch.topk(F.softmax(torch.einsum("bh, he -> be", tokens, rw), dim=-1), topk)
     return dispatch(tokens, top_idxs, num_experts, world_size, group)

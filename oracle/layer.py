@@ -170,3 +170,41 @@ def compact_from_padded(out: np.ndarray, recv_counts: np.ndarray) -> np.ndarray:
     gm = rows // W
     return np.concatenate([out[le, src * gm:src * gm + int(recv_counts[src, le])]
                            for le in range(El) for src in range(W)])
+
+
+# ---------------------------------------------------------------- router
+# utils.py:17-25: logits = einsum('bh,he->be', tokens, router) in bf16,
+# softmax over experts (bf16 result), top-k.  Restated with fp32
+# accumulation rounded once to bf16 for the logits, an fp32 softmax rounded
+# to bf16, and top-k ordered by (probability descending, expert ascending);
+# the reference's torch.topk leaves the order of equal values unspecified,
+# so ``topk_mismatches`` compares selections tie-aware.
+
+def router(tokens: np.ndarray, router_w: np.ndarray, k: int):
+    """Returns (logits, probs, top_vals, top_idxs): logits and probs are
+    bf16-valued float32 [T, E]; top_vals [T, k] float32, top_idxs [T, k] int64."""
+    x = np.asarray(tokens, np.float32)
+    r = np.asarray(router_w, np.float32)
+    T, E = x.shape[0], r.shape[1]
+    logits = _bf16_round(x @ r)
+    if T == 0:
+        return logits, logits.copy(), np.zeros((0, k), np.float32), np.zeros((0, k), np.int64)
+    e = np.exp(logits - logits.max(axis=-1, keepdims=True))
+    probs = _bf16_round(e / e.sum(axis=-1, keepdims=True))
+    order = np.lexsort((np.broadcast_to(np.arange(E), probs.shape), -probs), axis=-1)
+    ids = order[:, :k].astype(np.int64)
+    return logits, probs, np.take_along_axis(probs, ids, axis=-1), ids
+
+
+def topk_mismatches(ids: np.ndarray, vals: np.ndarray, probs: np.ndarray, ref_vals: np.ndarray,
+                    ulps: int = 0) -> int:
+    """Tokens whose selection is not a valid top-k of ``probs``: the ids
+    must be distinct, ``vals`` must equal the reference's sorted top values
+    and the probabilities the ids point at (both within ``ulps`` bf16 ulps)."""
+    ids = np.asarray(ids, np.int64)
+    tol = np.abs(ref_vals) * (ulps * 2.0 ** -8) if ulps else 0.0
+    picked = np.take_along_axis(probs, ids, axis=-1)
+    ok = (np.abs(vals - ref_vals) <= tol) & (np.abs(picked - ref_vals) <= tol)
+    s = np.sort(ids, axis=-1)
+    distinct = (s[:, 1:] != s[:, :-1]).all(axis=-1) if ids.shape[1] > 1 else np.ones(ids.shape[0], bool)
+    return int((~(ok.all(axis=-1) & distinct)).sum())

@@ -20,6 +20,12 @@ the reference.
    all-ranks max (the oracle's convention); the fixture stores the routing
    ids, counts, the reference's fp32 output and SHA-256 digests of the
    regenerated tokens and weights.
+3. router_golden.npz — the router of ``utils.gen_tensor`` (utils.py:17-25:
+   bf16 einsum of tokens and router matrix, softmax, top-k) run on CPU for
+   shapes whose expert count is a multiple of 8.  ``torch.einsum`` and
+   ``torch.topk`` are observed to record their operands and results: the
+   tokens, the router matrix, the bf16 logits, the bf16 probabilities and
+   the top-k values and ids.
 """
 from __future__ import annotations
 
@@ -91,6 +97,53 @@ def make_routing(ref: Path) -> dict:
     return out
 
 
+ROUTER_CASES = [  # (batch, seq, hidden, experts, topk, world, rank)
+    (1, 256, 64, 8, 2, 2, 0), (1, 128, 256, 16, 4, 2, 1), (1, 512, 128, 64, 6, 2, 0),
+    (1, 64, 512, 256, 8, 8, 3), (2, 64, 32, 8, 1, 1, 0),
+]
+
+
+def make_router(ref: Path) -> dict:
+    sys.path.insert(0, str(ref))
+    import utils as ref_utils  # the reference's utils.py
+
+    out = {}
+    real_einsum, real_topk = torch.einsum, torch.topk
+    for ci, (b, s, h, e, k, w, r) in enumerate(ROUTER_CASES):
+        seen = {}
+
+        def einsum_spy(eq, *ops, **kw):
+            res = real_einsum(eq, *ops, **kw)
+            seen.setdefault("einsum", (ops[0], ops[1], res))
+            return res
+
+        def topk_spy(x, *a, **kw):
+            res = real_topk(x, *a, **kw)
+            seen.setdefault("topk", (x, res[0], res[1]))
+            return res
+
+        torch.einsum, torch.topk = einsum_spy, topk_spy
+        try:
+            try:
+                ref_utils.gen_tensor(b, s, h, w, e, r, k)
+            except (RuntimeError, AssertionError):
+                pass  # bucketing after the router may need a GPU; the router ran first
+        finally:
+            torch.einsum, torch.topk = real_einsum, real_topk
+        tok, rmat, logits = seen["einsum"]
+        probs, vals, ids = seen["topk"]
+        p = f"c{ci}_"
+        out[p + "shape"] = np.array([b, s, h, e, k, w, r], np.int64)
+        out[p + "tokens"] = bf16_bits(tok)
+        out[p + "router"] = bf16_bits(rmat)
+        out[p + "logits"] = bf16_bits(logits)
+        out[p + "probs"] = bf16_bits(probs)
+        out[p + "top_vals"] = bf16_bits(vals)
+        out[p + "top_idxs"] = ids.numpy().astype(np.int16)
+    out["num_cases"] = np.array([len(ROUTER_CASES)], np.int64)
+    return out
+
+
 def _layer_rank(rank: int, world: int, port: int, ref: str, q) -> None:
     import torch.distributed as dist
     sys.path.insert(0, ref)
@@ -155,7 +208,8 @@ def main() -> int:
     ref = Path(a.reference)
     np.savez_compressed(HERE / "routing_golden.npz", **make_routing(ref))
     np.savez_compressed(HERE / "layer_golden.npz", **make_layer(ref))
-    for f in ("routing_golden.npz", "layer_golden.npz"):
+    np.savez_compressed(HERE / "router_golden.npz", **make_router(ref))
+    for f in ("routing_golden.npz", "layer_golden.npz", "router_golden.npz"):
         print(f, os.path.getsize(HERE / f), "bytes")
     return 0
 

@@ -197,3 +197,37 @@ def test_compact_layer_matches_reference_layer_outputs():
         ref = oracle.compact_from_padded(g[f"r{r}_out"], rcm)
         assert outs[r].shape == (int(rcm.sum()), wl.N)
         np.testing.assert_allclose(outs[r], ref, rtol=1e-5, atol=1e-5)
+
+
+def test_router_matches_reference_router():
+    """The router restatement against the reference's own router
+    (utils.py:17-25, run on CPU; golden): logits and probabilities bit for
+    bit (a rare logit may differ by one bf16 ulp through the summation
+    order), top-k values equal, and every selection a valid top-k of the
+    reference's probabilities (the reference's tiny router makes many
+    probabilities equal, and torch.topk orders equal values arbitrarily)."""
+    g = np.load(GOLDEN / "router_golden.npz")
+    f = oracle.bf16_bits_to_f32
+    for ci in range(int(g["num_cases"][0])):
+        p = f"c{ci}_"
+        b, s, h, e, k, w, r = (int(x) for x in g[p + "shape"])
+        logits, probs, vals, ids = oracle.router(f(g[p + "tokens"]), f(g[p + "router"]), k)
+        ref_logits, ref_probs, ref_vals = f(g[p + "logits"]), f(g[p + "probs"]), f(g[p + "top_vals"])
+        assert ids.shape == (b * s, k)
+        assert (logits == ref_logits).mean() > 0.999, ci
+        assert np.all(np.abs(logits - ref_logits) <= np.abs(ref_logits) * 2.0 ** -7), ci
+        assert np.array_equal(probs, ref_probs), ci
+        assert np.array_equal(vals, ref_vals), ci
+        assert oracle.topk_mismatches(ids, vals, ref_probs, ref_vals) == 0, ci
+        # and the reference's own selection passes the same check
+        assert oracle.topk_mismatches(g[p + "top_idxs"], ref_vals, ref_probs, ref_vals) == 0, ci
+
+
+def test_router_topk_order_and_ties():
+    x = np.eye(4, dtype=np.float32)
+    rw = np.array([[0, 1, 1, 0], [2, 0, 0, 0], [0, 0, 0, 0], [0, 0, 3, 1]], np.float32)
+    _, probs, vals, ids = oracle.router(x, rw, 2)
+    assert ids[0].tolist() == [1, 2]          # equal probabilities: ascending id
+    assert ids[1].tolist() == [0, 1]
+    assert ids[3].tolist() == [2, 3]
+    assert np.all(np.diff(vals, axis=-1) <= 0)
