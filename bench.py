@@ -337,6 +337,24 @@ def run_router_path(args) -> int:
     ms, clocks = time_device(ours, args.steps, args.warmup, sampler_device=local)
     ms_t, _ = time_device(torch_router, args.steps, args.warmup)
     ms, ms_t = max_over_ranks(ms), max_over_ranks(ms_t)
+    # The same calls replayed from CUDA graphs: device time without the host's
+    # per-launch cost (both are launch-bound when called eagerly).
+    graphs = {}
+    for name, fn in (("ours", ours), ("torch", torch_router)):
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                fn()
+        torch.cuda.current_stream().wait_stream(side)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            fn()
+        graphs[name] = gr
+    ms_g, _ = time_device(graphs["ours"].replay, args.steps, args.warmup)
+    ms_tg, _ = time_device(graphs["torch"].replay, args.steps, args.warmup)
+    ms_g, ms_tg = max_over_ranks(ms_g), max_over_ranks(ms_tg)
+    graphs.clear()
     peaks, src = load_peaks()
     flops = 2.0 * wl.T * wl.H * wl.E
     hbm = wl.T * wl.H * 2 + wl.H * wl.E * 2 + 2 * wl.T * wl.E * 2 + wl.T * K * 12
@@ -350,8 +368,10 @@ def run_router_path(args) -> int:
             "config": {"workload": wl.name + "+router", "tokens_per_rank": wl.T, "hidden": wl.H, "experts": wl.E,
                        "top_k": K},
             "top_vals_match_torch": vals_equal, "torch_us": ms_t * 1e3,
+            "graph_us": ms_g * 1e3, "torch_graph_us": ms_tg * 1e3,
             "roofline": {"bound": "hbm" if hbm / (hbm_peak * 1e9) > flops / (peak * 1e12) else "tensor",
-                         "roofline_us": t_roof * 1e6, "frac": t_roof / (ms * 1e-3), "peak_source": src,
+                         "roofline_us": t_roof * 1e6, "frac": t_roof / (ms * 1e-3),
+                         "frac_graph": t_roof / (ms_g * 1e-3), "peak_source": src,
                          "flops": flops, "algorithmic_hbm_bytes": hbm},
             "gpu_launches": 3 * args.steps,  # count word, logits GEMM, softmax/top-k
             "clocks": clocks}

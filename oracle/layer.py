@@ -202,7 +202,7 @@ def topk_mismatches(ids: np.ndarray, vals: np.ndarray, probs: np.ndarray, ref_va
     must be distinct, ``vals`` must equal the reference's sorted top values
     and the probabilities the ids point at (both within ``ulps`` bf16 ulps)."""
     ids = np.asarray(ids, np.int64)
-    tol = np.abs(ref_vals) * (ulps * 2.0 ** -8) if ulps else 0.0
+    tol = np.abs(ref_vals) * (ulps * 2.0 ** -7) if ulps else 0.0  # a bf16 ulp is 2^-8..2^-7 of the value
     picked = np.take_along_axis(probs, ids, axis=-1)
     ok = (np.abs(vals - ref_vals) <= tol) & (np.abs(picked - ref_vals) <= tol)
     s = np.sort(ids, axis=-1)
