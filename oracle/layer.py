@@ -185,15 +185,21 @@ def router(tokens: np.ndarray, router_w: np.ndarray, k: int):
     bf16-valued float32 [T, E]; top_vals [T, k] float32, top_idxs [T, k] int64."""
     x = np.asarray(tokens, np.float32)
     r = np.asarray(router_w, np.float32)
-    T, E = x.shape[0], r.shape[1]
     logits = _bf16_round(x @ r)
+    return (logits,) + softmax_topk(logits, k)
+
+
+def softmax_topk(logits: np.ndarray, k: int):
+    """The router after its GEMM: (probs, top_vals, top_idxs) of bf16-valued logits."""
+    logits = np.asarray(logits, np.float32)
+    T, E = logits.shape
     if T == 0:
-        return logits, logits.copy(), np.zeros((0, k), np.float32), np.zeros((0, k), np.int64)
+        return logits.copy(), np.zeros((0, k), np.float32), np.zeros((0, k), np.int64)
     e = np.exp(logits - logits.max(axis=-1, keepdims=True))
     probs = _bf16_round(e / e.sum(axis=-1, keepdims=True))
     order = np.lexsort((np.broadcast_to(np.arange(E), probs.shape), -probs), axis=-1)
     ids = order[:, :k].astype(np.int64)
-    return logits, probs, np.take_along_axis(probs, ids, axis=-1), ids
+    return probs, np.take_along_axis(probs, ids, axis=-1), ids
 
 
 def topk_mismatches(ids: np.ndarray, vals: np.ndarray, probs: np.ndarray, ref_vals: np.ndarray,
