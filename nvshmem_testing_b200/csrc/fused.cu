@@ -110,6 +110,7 @@ struct Params {
   int general;
   int64_t send_rows, out_rows;
   int tile_cap;  // most rows per tile (multiple of 16, <= kMaxTileRows)
+  int kstagger;  // tile t walks K from k-block t % kblocks (many tiles sharing one weight slice)
   int32_t* status_host;
   uint64_t* trace;  // MOE_EP_TRACE_WORDS per CTA, or null
 };
@@ -583,9 +584,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t b_bytes = 2 * uint32_t(8 << bm) * BK * 2;  // two 64-K halves
         const uint32_t tx = uint32_t(nb_mine + nb_peer) * kABox + 2 * b_bytes;
         bool stop = false;
+        // With k staggering, tile t starts its K loop at k-block t % kblocks
+        // (the MMA's accumulate flag follows the iteration, not the block).
+        const int rot = p.kstagger ? t % s.kblocks : 0;
         for (int kb = 0; kb < s.kblocks; ++kb, ++it) {
           const int st = it % kStages;
           const uint32_t round = it / kStages;
+          const int kc = kb + rot < s.kblocks ? kb + rot : kb + rot - s.kblocks;
           const uint64_t te0 = TRACE_NOW(p);
           if (!mbar_wait(&sm.empty[st], (round & 1) ^ 1, pipe_bound, sm)) {
             if (!aborted(sm)) raise_error(p, sm, kTimeout, kSitePipe, 0);
@@ -601,13 +606,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           // of 128, one box for the rows: the TMA engine overlaps few boxes
           // at a time, so fewer, larger boxes keep more bytes in flight.
           if (p.w4) {
-            if (nb_mine) tma_load_4d_pair(&tm_w4, bar, a_dst, 0, kb * KB, f_mine / 64, tl.le);
+            if (nb_mine) tma_load_4d_pair(&tm_w4, bar, a_dst, 0, kc * KB, f_mine / 64, tl.le);
           } else {
             for (int j = 0; j < nb_mine; ++j)
-              tma_load_3d_pair(&tm_w, bar, a_dst + j * kABox, f_mine + 64 * j, kb * KB, tl.le);
+              tma_load_3d_pair(&tm_w, bar, a_dst + j * kABox, f_mine + 64 * j, kc * KB, tl.le);
           }
-          tma_load_2d_pair(&rm.m[bm], bar, b_dst, kb * KB, int(row_base));
-          tma_load_2d_pair(&rm.m[bm], bar, b_dst + kBHalf, kb * KB + BK, int(row_base));
+          tma_load_2d_pair(&rm.m[bm], bar, b_dst, kc * KB, int(row_base));
+          tma_load_2d_pair(&rm.m[bm], bar, b_dst + kBHalf, kc * KB + BK, int(row_base));
           sm.fills[st] += 1;
         }
         if (stop) break;
@@ -1033,6 +1038,7 @@ int launch_fused(const moe_ep_run_params* a, const FusedMode& m, cudaStream_t st
   p.off_rflag = L.off_rflag;
   p.general = m.general;
   p.tile_cap = m.tile_cap > 0 ? m.tile_cap : kMaxTileRows;
+  p.kstagger = m.kstagger;
   p.send_rows = m.send_rows;
   p.out_rows = m.out_rows;
   p.status_host = a->status_host;

@@ -81,6 +81,7 @@ struct FusedMode {
   int64_t send_rows = 0;  // compact mode: rows of tokens
   int64_t out_rows = 0;   // compact mode: rows of out
   int tile_cap = 0;       // most rows per GEMM tile (multiple of 16); 0 = 256
+  int kstagger = 0;       // stagger each tile's first k-block (tiles that share weights)
 };
 int launch_fused(const moe_ep_run_params* a, const FusedMode& m, cudaStream_t stream);
 

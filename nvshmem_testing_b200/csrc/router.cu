@@ -207,6 +207,9 @@ extern "C" int moe_router(const void* x, int64_t T, int32_t H, const void* route
   cap = (cap + 15) / 16 * 16;
   FusedMode m;
   m.tile_cap = int(cap < 16 ? 16 : (cap > 256 ? 256 : cap));
+  // Every tile reads the same router matrix: start each one at a different
+  // k-block so the CTAs do not all request the same lines at once.
+  m.kstagger = 1;
   const int rc = launch_fused(&p, m, s);
   if (rc != kOk) return rc;
   const auto* lg = static_cast<const __nv_bfloat16*>(logits);
