@@ -300,7 +300,9 @@ __device__ void build_schedule(const Params& p, Sched& s, Smem& sm) {
   const int W = p.W, El = p.El, me = p.me, tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const uint32_t par = p.epoch & 1u;
-  const int32_t* cm = reinterpret_cast<const int32_t*>(p.local + p.off_cmat) + size_t(par) * W * W * El;
+  // One rank reads its own recv_counts (nothing was exchanged).
+  const int32_t* cm = W == 1 ? p.recv_counts
+                             : reinterpret_cast<const int32_t*>(p.local + p.off_cmat) + size_t(par) * W * W * El;
   // cmat[owner][src][le]: rows src sends to owner's local expert le.
   auto C = [&](int owner, int src, int le) { return cm[(size_t(owner) * W + src) * El + le]; };
   const int nfeat = (p.N + kFeatPair - 1) / kFeatPair;
@@ -486,8 +488,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = sm.tmem_base;
 
   // ---- count exchange: CTA 0 publishes this rank's recv_counts block to
-  // every rank; every CTA then waits for all W blocks.
-  if (blockIdx.x == 0 && warp == kWarpPush0) {
+  // every rank; every CTA then waits for all W blocks.  One rank has nothing
+  // to exchange: the schedule reads recv_counts directly, and each CTA only
+  // waits until the call that last used this epoch parity has finished.
+  if (W > 1 && blockIdx.x == 0 && warp == kWarpPush0) {
     for (int d = 0; d < W; ++d) {
       unsigned char* peer = reinterpret_cast<unsigned char*>(p.peers[d]);
       int go = 1;
@@ -506,7 +510,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   if (tid == 0) {
-    for (int q = 0; q < W; ++q) {
+    if (W == 1) {
+      if (p.epoch > 2 && !wait_epoch(at_u32(p.local, p.off_free), p.epoch - 2, p.timeout_ns, sm))
+        raise_error(p, sm, kTimeout, kSiteFree, 0);
+    }
+    for (int q = 0; q < W && W > 1; ++q) {
       if (!wait_epoch(at_u32(p.local, p.off_cflag) + par * W + q, p.epoch, p.timeout_ns, sm)) {
         raise_error(p, sm, kTimeout, kSiteCounts, q);
         break;
