@@ -310,6 +310,85 @@ def run_reference_arm(args) -> int:
     return 0
 
 
+def run_mlp_path(args) -> int:
+    """The full expert MLP (``mlp.run``: compact exchange + [gate|up] GEMM,
+    SwiGLU, down GEMM) against NCCL a2a + bmm(w13) + silu*up + bmm(w2) over
+    padded rows, on the same inputs.  FFN width F = the workload's out_dim."""
+    from nvshmem_testing_b200 import mlp
+
+    rank, world, local = init_dist(args.gpus)
+    dev = torch.device("cuda", local)
+    wl = workloads.get(args.workload, dtype=torch.bfloat16, **overrides(args))
+    El, H, F = wl.local_experts(world), wl.H, wl.N
+    tokens = workloads.tokens(wl, rank, device=dev)
+    ids = workloads.top_idxs(wl, rank).to(dev)
+    g = torch.Generator(device=dev).manual_seed(wl.seed + 10086 + rank)
+    w13 = (0.02 * torch.randn(El, H, 2 * F, generator=g, device=dev)).to(torch.bfloat16)
+    w2 = (0.02 * torch.randn(El, F, H, generator=g, device=dev)).to(torch.bfloat16)
+    coalesced, chunk, lengths = utils.dispatch(tokens, ids, wl.E, world)
+    compact, total, _ = utils.dispatch(tokens, ids, wl.E, world, general_a2a=True)
+    counts = torch.tensor(lengths, dtype=torch.int32, device=dev)
+    recv_counts = utils.recv_counts_from(counts, world)
+    gm = chunk // El
+    rc_cpu = recv_counts.cpu()
+    rows_in = int(rc_cpu.sum())
+    remote_in = rows_in - int(rc_cpu[rank].sum())
+    remote_out = int(counts.view(world, El).sum()) - int(counts.view(world, El)[rank].sum())
+
+    def ours():
+        return mlp.run(rank, compact, total, world, w13, w2, recv_counts, max_count=gm, recv_rows=rows_in)
+
+    def nccl():
+        a = nccl_a2a_bmm(coalesced, chunk, world, w13)
+        h = torch.nn.functional.silu(a[..., :F]) * a[..., F:]
+        return torch.bmm(h, w2)
+
+    y = ours()
+    ref = nccl()
+    ref = torch.cat([ref[le, src * gm:src * gm + int(rc_cpu[src, le])] for le in range(El) for src in range(world)])
+    scale = float(ref.float().abs().max()) if ref.numel() else 1.0
+    ok = bool(torch.allclose(y.float(), ref.float(), rtol=1e-2, atol=1e-2 * scale))
+    del ref, y
+    ms, clocks = time_device(ours, args.steps, args.warmup, sampler_device=local)
+    ms_n, _ = time_device(nccl, max(args.steps // 3, 5), args.warmup)
+    ms, ms_n = max_over_ranks(ms), max_over_ranks(ms_n)
+    flops_rank = 6.0 * rows_in * H * F
+    flops_total = sum_over_ranks(flops_rank)
+    peaks, src = load_peaks()
+    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    hbm_peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    # weights once; rows in, the [gate|up] rows out and back in, h out and in, y out
+    hbm = 3 * El * H * F * 2 + rows_in * (H * 2 + 2 * F * 2 * 2 + F * 2 * 2 + H * 2) + \
+        (remote_in + remote_out) * H * 2
+    t_gemm = flops_rank / (peak * 1e12) * 1e6
+    t_hbm = hbm / (hbm_peak * 1e9) * 1e6
+    t_link = max(remote_in, remote_out) * H * 2 / (NVLINK_GBS * 1e9) * 1e6
+    roof = max_over_ranks(max(t_gemm, t_hbm, t_link))
+    bound = "hbm" if t_hbm > t_gemm else "tensor"
+    line = {"metric": "fused dispatch + full expert MLP (gate/up, SwiGLU, down) µs/layer & TFLOP/s vs NCCL",
+            "path": "mlp", "value": flops_total / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "us_per_layer": ms * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded)",
+            "config": {"workload": wl.name + "+mlp", "tokens_per_rank": wl.T, "hidden": H, "experts": wl.E,
+                       "local_experts": El, "top_k": wl.K, "ffn": F, "routing": wl.routing, "gm": gm,
+                       "parallelism": f"ep{world}"},
+            "parity_vs_nccl_allclose": ok,
+            "roofline": {"bound": bound, "layer_roofline_us": roof, "layer_frac": roof / (ms * 1e3),
+                         "bounds_us": {"tensor": t_gemm, "hbm": t_hbm, "nvlink": t_link},
+                         "algorithmic_hbm_bytes": hbm, "peak_source": src},
+            "nccl_mlp": {"us_per_layer": ms_n * 1e3, "value": flops_total / (ms_n * 1e-3) / 1e12,
+                         "what": "NCCL a2a + bmm(w13) + silu*up + bmm(w2) over padded rows"},
+            "gpu_launches": 3 * args.steps, "clocks": clocks}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    from nvshmem_testing_b200 import symm
+    symm.release_all()
+    dist.destroy_process_group()
+    return 0
+
+
 def run_router_path(args) -> int:
     """The router (``utils.router``: tcgen05 logits GEMM + softmax/top-k
     kernel) on one rank's tokens, against torch's einsum + softmax + topk
@@ -528,10 +607,12 @@ def main(argv=None) -> int:
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-nccl", action="store_true")
-    ap.add_argument("--path", choices=["dispatch_gemm", "general", "combine", "router"], default="dispatch_gemm",
+    ap.add_argument("--path", choices=["dispatch_gemm", "general", "combine", "router", "mlp"],
+                    default="dispatch_gemm",
                     help="dispatch_gemm: the reference's path (default); general: the unpadded exchange "
                          "(general_a2a=True); combine: with return + top-k combine; router: the router "
-                         "(einsum, softmax, top-k) before the path")
+                         "(einsum, softmax, top-k) before the path; mlp: the full gated expert MLP "
+                         "(FFN width = the workload's out_dim)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -541,6 +622,8 @@ def main(argv=None) -> int:
         return run_combine_path(args)
     if args.path == "router":
         return run_router_path(args)
+    if args.path == "mlp":
+        return run_mlp_path(args)
 
     rank, world, local = init_dist(args.gpus)
     dev = torch.device("cuda", local)

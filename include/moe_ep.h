@@ -18,6 +18,8 @@
  *   moe_ep_run                  alltoall_persistent_gemm.py:207-309 (run:
  *                               peer copies + flags + fused grouped GEMM) and
  *                               baseline.py:8-56 (same output contract)
+ *   moe_swiglu                  the full expert MLP's activation (the
+ *                               reference's expert is one GEMM, baseline.py:50)
  *   moe_router                  utils.py:17-25 (router logits einsum, softmax,
  *                               top-k: the step before the reference's path)
  *   moe_pack_compact,           the general (unbalanced) all-to-all that
@@ -265,6 +267,15 @@ typedef struct moe_ep_combine_params {
 } moe_ep_combine_params;
 
 int moe_ep_run_combine(const moe_ep_run_params* run, const moe_ep_combine_params* combine, void* stream);
+
+/* ---------------------------------------------------------------- expert MLP
+ * The activation between the expert MLP's two GEMMs (the reference's expert
+ * is a single GEMM, baseline.py:50): a [rows, 2F] bf16 holds [gate | up] per
+ * row; h [rows, F] bf16 = silu(gate) * up, computed in fp32 with
+ * silu(g) = g / (1 + exp(-g)).  Requires F % 8 == 0 and 16-byte aligned
+ * buffers.  The GEMMs around it are moe_ep_run_compact calls (the exchange
+ * with w13 [El, H, 2F], then one rank's local call with w2 [El, F, H]). */
+int moe_swiglu(const void* a, int64_t rows, int32_t F, void* h, void* stream);
 
 /* Copy the workspace status word to the host (synchronous). */
 int moe_ep_read_status(uint64_t local_base, const moe_ep_layout* layout, uint32_t* out);

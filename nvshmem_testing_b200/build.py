@@ -22,7 +22,7 @@ CSRC = PKG / "csrc"
 INCLUDE = ROOT / "include"
 OUT_DIR = PKG / "_lib"
 LIB = OUT_DIR / "libmoe_ep.so"
-SOURCES = ["route.cu", "fused.cu", "combine.cu", "router.cu", "driver.cu", "capi.cu", "noalloc.cu"]
+SOURCES = ["route.cu", "fused.cu", "combine.cu", "router.cu", "mlp.cu", "driver.cu", "capi.cu", "noalloc.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

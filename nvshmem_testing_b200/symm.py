@@ -133,9 +133,14 @@ class SymmetricWorkspace:
         N.check(L.moe_ep_workspace_reset(self.base, ctypes.byref(self.layout), ctypes.c_void_p(stream.cuda_stream)),
                 "moe_ep_workspace_reset")
         torch.cuda.synchronize(dev)
+        # One rank has no peers: no rendezvous (and no collective on `group`,
+        # so a rank may hold a private one-rank workspace for local work).
         try:
-            tag = _broadcast_token(group)
-            peer_fds = exchange_fds(fd.value, rank, key.W, tag, lambda: _barrier(group))
+            if key.W > 1:
+                tag = _broadcast_token(group)
+                peer_fds = exchange_fds(fd.value, rank, key.W, tag, lambda: _barrier(group))
+            else:
+                peer_fds = {}
         finally:
             os.close(fd.value)
         bases = [0] * key.W
@@ -158,7 +163,8 @@ class SymmetricWorkspace:
         # Mapped pinned word the kernels latch device-side errors into.
         self.status_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
         self.epoch = 0
-        _barrier(group)  # every rank has zeroed and mapped before the first call
+        if key.W > 1:
+            _barrier(group)  # every rank has zeroed and mapped before the first call
 
     def next_epoch(self) -> int:
         self.epoch += 1

@@ -214,3 +214,32 @@ def topk_mismatches(ids: np.ndarray, vals: np.ndarray, probs: np.ndarray, ref_va
     s = np.sort(ids, axis=-1)
     distinct = (s[:, 1:] != s[:, :-1]).all(axis=-1) if ids.shape[1] > 1 else np.ones(ids.shape[0], bool)
     return int((~(ok.all(axis=-1) & distinct)).sum())
+
+
+# ---------------------------------------------------------------- expert MLP
+# The gated expert MLP around the exchange (the reference's expert is the
+# single GEMM of baseline.py:50): a = x @ [W_gate | W_up] (bf16 out),
+# h = silu(gate) * up (fp32, bf16 out), y = h @ W_down (fp32).
+
+def mlp_compact(send: list[np.ndarray], all_counts: list[np.ndarray], w13: list[np.ndarray],
+                w2: list[np.ndarray]) -> list[np.ndarray]:
+    """Per rank r: [rows received, H] in the compact (le, src) cell order of
+    ``compact_layer``; w13[r] [El, H, 2F], w2[r] [El, F, H]."""
+    from .routing import recv_counts_matrix
+    W = len(send)
+    El = w13[0].shape[0]
+    F = w13[0].shape[2] // 2
+    first = compact_layer(send, all_counts, w13)
+    outs = []
+    for r in range(W):
+        a = _bf16_round(first[r])
+        g, u = a[:, :F], a[:, F:]
+        h = _bf16_round((g / (1.0 + np.exp(-g))) * u)
+        rcm = recv_counts_matrix(all_counts, r, W)
+        per_expert = rcm.sum(axis=0)
+        starts = np.concatenate([[0], np.cumsum(per_expert)])
+        y = np.zeros((h.shape[0], w2[r].shape[2]), np.float32)
+        for le in range(El):
+            y[starts[le]:starts[le + 1]] = h[starts[le]:starts[le + 1]] @ w2[r][le].astype(np.float32)
+        outs.append(y)
+    return outs

@@ -231,3 +231,24 @@ def test_router_topk_order_and_ties():
     assert ids[1].tolist() == [0, 1]
     assert ids[3].tolist() == [2, 3]
     assert np.all(np.diff(vals, axis=-1) <= 0)
+
+
+def test_mlp_oracle_reduces_to_the_reference_layer():
+    """The MLP restatement is the compact layer (pinned to the reference's
+    outputs above) followed by SwiGLU and a per-expert GEMM: with an
+    identity-like W_down its output is the activation h itself."""
+    rng = np.random.default_rng(5)
+    W, El, H, F = 2, 2, 16, 8
+    counts = [np.array([3, 0, 2, 4]), np.array([1, 5, 0, 2])]
+    send = [rng.standard_normal((int(c.sum()), H)).astype(np.float32) for c in counts]
+    w13 = [rng.standard_normal((El, H, 2 * F)).astype(np.float32) * 0.3 for _ in range(W)]
+    eye = [np.stack([np.eye(F, H, dtype=np.float32)] * El) for _ in range(W)]
+    y = oracle.mlp_compact(send, counts, w13, eye)
+    a = oracle.compact_layer(send, counts, w13)
+    bf = lambda z: oracle.bf16_bits_to_f32(oracle.f32_to_bf16_bits(z))
+    for r in range(W):
+        ab = bf(a[r])
+        h = bf(ab[:, :F] / (1 + np.exp(-ab[:, :F])) * ab[:, F:])
+        np.testing.assert_allclose(y[r][:, :F], h, rtol=1e-6, atol=1e-6)
+        assert not y[r][:, F:].any()
+        assert y[r].shape[0] == int(oracle.recv_counts_matrix(counts, r, W).sum())
