@@ -55,6 +55,22 @@ def _counts_worker(rank, world, port, q):
         q.put((rank, "error", traceback.format_exc()))
 
 
+def _bound_worker(rank, world, port, q):
+    try:
+        import torch
+        import torch.distributed as dist
+        from nvshmem_testing_b200 import alltoall_persistent_gemm as apg
+
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+        rc = torch.tensor([[3, 0], [7, 1]]) if rank == 0 else torch.tensor([[2, 9], [0, 4]])
+        rows, bound = apg._general_bound(rc, None)
+        zeros = apg._general_bound(torch.zeros(2, 2, dtype=torch.int32), None)
+        dist.destroy_process_group()
+        q.put((rank, "ok", (rows, bound, zeros)))
+    except Exception:
+        q.put((rank, "error", traceback.format_exc()))
+
+
 def _run(target, world):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
@@ -85,3 +101,15 @@ def test_count_exchange_matches_oracle():
     for r, (kind, payload) in res.items():
         assert kind == "ok", payload
         assert payload is True
+
+
+def test_general_bound_is_all_reduced():
+    """The unpadded exchange sizes its buffers by the largest count over the
+    group (all-reduced MAX) and its output by this rank's own rows."""
+    res = _run(_bound_worker, 2)
+    for r, (kind, payload) in res.items():
+        assert kind == "ok", payload
+        rows, bound, zeros = payload
+        assert rows == (11 if r == 0 else 15)
+        assert bound == 9
+        assert zeros == (0, 1)  # empty counts: bound at least 1
