@@ -61,7 +61,7 @@ namespace moe {
 
 constexpr int BK = 64;                          // K of one 128-byte swizzle atom (bf16)
 constexpr int KB = 128;                         // K per pipeline stage (two atoms)
-constexpr int kStages = 3;                      // the wide pipeline (see the variants below)
+constexpr int kStages = 3;
 constexpr int kFeatPair = 256;                  // output features per pair tile (MMA M)
 constexpr int kFeatCta = 128;                   // features per CTA (TMEM lanes)
 constexpr int kMaxTileRows = 256;               // rows per tile (MMA N)
@@ -72,10 +72,13 @@ constexpr int kThreads = (2 + kEpiWarps + kPushWarps) * 32;
 constexpr int kPushThreads = kPushWarps * 32;
 constexpr uint32_t kABox = 64 * KB * 2;                       // 16 KB: 64 features x 128 K
 constexpr uint32_t kABytes = kFeatCta * KB * 2;               // 32 KB
-// Per pipeline variant (in the kernel): B half = MAXROWS/2 rows x 64 K, stage =
-// kABytes + 2 B halves, two accumulators of MAXROWS TMEM columns.
+constexpr uint32_t kBHalf = (kMaxTileRows / 2) * BK * 2;      // 16 KB: 128 rows x 64 K
+constexpr uint32_t kBBytesMax = 2 * kBHalf;                   // 32 KB: 128 rows x 128 K
+constexpr uint32_t kStageBytes = kABytes + kBBytesMax;        // 64 KB
 constexpr int kMaxCells = 512;                  // W * El
 constexpr int kMaxLocalExperts = 256;
+constexpr uint32_t kAccCols = kMaxTileRows;
+constexpr uint32_t kTmemCols = 2 * kAccCols;
 constexpr int kGoSlots = 8;                     // > kStages: the leader runs at most kStages k-blocks ahead
 constexpr int kRowMaps = 5;                     // B boxes of 8, 16, 32, 64, 128 rows
 constexpr int kNamedBarPush = 1;
@@ -142,16 +145,9 @@ struct Sched {
   int ooff[kMaxCells + 1];                // compact mode: [le][src] first output row of the cell
 };
 
-// Pipeline variants: the wide one (3 x 64 KB stages, tiles up to 256 rows)
-// and the narrow one (4 x 48 KB stages, tiles up to 128 rows) for launches
-// whose tiles are short anyway: 192 KB instead of 144 KB of loads in flight.
-constexpr int kNarrowStages = 4;
-constexpr int kNarrowRows = 128;
-constexpr int kMaxStages = kNarrowStages;
-
 struct Smem {
-  uint64_t full[kMaxStages];   // leader: both CTAs' bytes for the stage landed
-  uint64_t empty[kMaxStages];  // each CTA: the pair MMA finished reading the stage
+  uint64_t full[kStages];   // leader: both CTAs' bytes for the stage landed
+  uint64_t empty[kStages];  // each CTA: the pair MMA finished reading the stage
   uint64_t tfull[2];        // each CTA: accumulator ready
   uint64_t tempty[2];       // leader: both CTAs' epilogues drained the accumulator
   uint64_t go[kGoSlots];    // peer: the leader's verdict for a tile
@@ -160,8 +156,8 @@ struct Smem {
   uint32_t tmem_base;
   int abort_flag;
   int push_item;
-  uint32_t fills[kMaxStages];
-  uint32_t cons[kMaxStages];
+  uint32_t fills[kStages];
+  uint32_t cons[kStages];
 };
 
 __device__ __forceinline__ uint32_t* at_u32(unsigned char* base, uint64_t off) {
@@ -440,18 +436,10 @@ __device__ __forceinline__ unsigned char* ret_row_ptr(const Sched& s, const Para
          ((int64_t(p.me) * p.El + tl.le) * p.gm + i) * int64_t(p.N) * 2;
 }
 
-template <int STAGES, int MAXROWS>
 __global__ void __launch_bounds__(kThreads, 1)
     fused_ep_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_w4,
                     const __grid_constant__ RowMaps rows_local,
                     const __grid_constant__ RowMaps rows_remote, const Params p) {
-  // This variant's pipeline shape (the names hide the wide defaults).
-  constexpr int kStages = STAGES;
-  constexpr uint32_t kBHalf = (MAXROWS / 2) * BK * 2;       // MAXROWS/2 rows x 64 K
-  constexpr uint32_t kStageBytes = kABytes + 2 * kBHalf;
-  constexpr uint32_t kAccCols = MAXROWS;
-  constexpr uint32_t kTmemCols = 2 * kAccCols;
-  static_assert(STAGES <= kMaxStages && STAGES < kGoSlots, "stage count");
   extern __shared__ unsigned char smem_dyn[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
   unsigned char* stage_mem = base;  // kStages * kStageBytes, 1024-aligned
@@ -967,15 +955,15 @@ struct DeviceLaunchInfo {
   bool ready;
   int grid;
 };
-static DeviceLaunchInfo g_launch_info[2][kMaxDevices];  // [narrow][device]
+static DeviceLaunchInfo g_launch_info[kMaxDevices];
 
-constexpr size_t smem_plan(int stages, int rows) {
-  return 1024 + size_t(stages) * (kABytes + size_t(rows) * BK * 2) + kEpiStageBytes + sizeof(Sched) + sizeof(Smem);
-}
 // The whole shared-memory plan must fit the 227 KB a CTA may opt in to.
-static_assert(smem_plan(kStages, kMaxTileRows) <= 227 * 1024, "wide plan exceeds 227 KB");
-static_assert(smem_plan(kNarrowStages, kNarrowRows) <= 227 * 1024, "narrow plan exceeds 227 KB");
+static_assert(1024 + size_t(kStages) * kStageBytes + kEpiStageBytes + sizeof(Sched) + sizeof(Smem) <= 227 * 1024,
+              "shared memory plan exceeds 227 KB");
 
+size_t fused_smem_bytes() {
+  return 1024 + size_t(kStages) * kStageBytes + kEpiStageBytes + sizeof(Sched) + sizeof(Smem);
+}
 
 // m.ret_rows > 0 selects return mode: output rows go to the source ranks'
 // return regions (ret_rows rows of out_dim bf16 each, at least W*El*gm) and
@@ -1064,15 +1052,10 @@ int launch_fused(const moe_ep_run_params* a, const FusedMode& m, cudaStream_t st
   p.status_host = a->status_host;
   p.trace = a->trace;
 
-  // The narrow pipeline where tiles are short anyway: capped tiles, or one
-  // rank whose buckets are small (its tiles are the buckets).
-  const bool narrow = (m.tile_cap > 0 && m.tile_cap <= kNarrowRows) || (W == 1 && a->gm <= 2 * kNarrowRows);
-  if (narrow) p.tile_cap = std::min(p.tile_cap, kNarrowRows);
-  auto kernel = narrow ? fused_ep_kernel<kNarrowStages, kNarrowRows> : fused_ep_kernel<kStages, kMaxTileRows>;
-  const size_t smem = narrow ? smem_plan(kNarrowStages, kNarrowRows) : smem_plan(kStages, kMaxTileRows);
+  const size_t smem = fused_smem_bytes();
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return kCudaErr;
-  DeviceLaunchInfo& info = g_launch_info[narrow ? 1 : 0][dev];
+  DeviceLaunchInfo& info = g_launch_info[dev];
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1088,18 +1071,18 @@ int launch_fused(const moe_ep_run_params* a, const FusedMode& m, cudaStream_t st
     // Once per device: opt in to the shared memory size and size the
     // persistent grid to the CTA pairs that can be resident together.
     int sms = 0, clusters = 0;
-    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+    if (cudaFuncSetAttribute(fused_ep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
       return kCudaErr;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return kCudaErr;
     cfg.gridDim = dim3(unsigned(sms & ~1), 1, 1);
-    if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess || clusters < 1)
+    if (cudaOccupancyMaxActiveClusters(&clusters, fused_ep_kernel, &cfg) != cudaSuccess || clusters < 1)
       return kCudaErr;
     info.grid = 2 * std::min(clusters, sms / 2);
     info.ready = true;
   }
   const int grid = a->num_ctas > 0 ? int(a->num_ctas) : info.grid;
   cfg.gridDim = dim3(unsigned(grid), 1, 1);
-  if (cudaLaunchKernelEx(&cfg, kernel, tw, tw4, rl, rr, p) != cudaSuccess) return kCudaErr;
+  if (cudaLaunchKernelEx(&cfg, fused_ep_kernel, tw, tw4, rl, rr, p) != cudaSuccess) return kCudaErr;
   return cudaGetLastError() == cudaSuccess ? kOk : kCudaErr;
 }
 
