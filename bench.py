@@ -335,7 +335,15 @@ def run_mlp_path(args) -> int:
     remote_in = rows_in - int(rc_cpu[rank].sum())
     remote_out = int(counts.view(world, El).sum()) - int(counts.view(world, El)[rank].sum())
 
+    w13f = mlp.fuse_gate_up(w13) if F % 128 == 0 else None
+
     def ours():
+        if w13f is not None:  # activation in the first GEMM's epilogue
+            return mlp.run(rank, compact, total, world, w13f, w2, recv_counts, max_count=gm, recv_rows=rows_in,
+                           w13_fused=True)
+        return mlp.run(rank, compact, total, world, w13, w2, recv_counts, max_count=gm, recv_rows=rows_in)
+
+    def ours_separate():
         return mlp.run(rank, compact, total, world, w13, w2, recv_counts, max_count=gm, recv_rows=rows_in)
 
     def nccl():
@@ -350,8 +358,9 @@ def run_mlp_path(args) -> int:
     ok = bool(torch.allclose(y.float(), ref.float(), rtol=1e-2, atol=1e-2 * scale))
     del ref, y
     ms, clocks = time_device(ours, args.steps, args.warmup, sampler_device=local)
+    ms_s, _ = time_device(ours_separate, max(args.steps // 3, 5), args.warmup)
     ms_n, _ = time_device(nccl, max(args.steps // 3, 5), args.warmup)
-    ms, ms_n = max_over_ranks(ms), max_over_ranks(ms_n)
+    ms, ms_s, ms_n = max_over_ranks(ms), max_over_ranks(ms_s), max_over_ranks(ms_n)
     flops_rank = 6.0 * rows_in * H * F
     flops_total = sum_over_ranks(flops_rank)
     peaks, src = load_peaks()
@@ -377,9 +386,10 @@ def run_mlp_path(args) -> int:
             "roofline": {"bound": bound, "layer_roofline_us": roof, "layer_frac": roof / (ms * 1e3),
                          "bounds_us": {"tensor": t_gemm, "hbm": t_hbm, "nvlink": t_link},
                          "algorithmic_hbm_bytes": hbm, "peak_source": src},
+            "fused_swiglu": w13f is not None, "separate_swiglu_us": ms_s * 1e3,
             "nccl_mlp": {"us_per_layer": ms_n * 1e3, "value": flops_total / (ms_n * 1e-3) / 1e12,
                          "what": "NCCL a2a + bmm(w13) + silu*up + bmm(w2) over padded rows"},
-            "gpu_launches": 3 * args.steps, "clocks": clocks}
+            "gpu_launches": (2 if w13f is not None else 3) * args.steps, "clocks": clocks}
     if rank == 0:
         print(json.dumps(line), flush=True)
     dist.barrier()

@@ -277,6 +277,15 @@ int moe_ep_run_combine(const moe_ep_run_params* run, const moe_ep_combine_params
  * with w13 [El, H, 2F], then one rank's local call with w2 [El, F, H]). */
 int moe_swiglu(const void* a, int64_t rows, int32_t F, void* h, void* stream);
 
+/* moe_ep_run_compact with the activation in the GEMM's epilogue: the first
+ * GEMM of the expert MLP writing h = silu(gate) * up directly, so the
+ * [gate | up] rows never reach memory.  `weights` is w13 in the fused layout
+ * (mlp.fuse_gate_up): per 256 columns, 64 gate, the 64 matching up, 64
+ * gate, 64 up (one CTA's 128 features each); out_dim = 2F with
+ * 2F % 256 == 0; out is [out_rows, F], same row order as moe_ep_run_compact.
+ * Each value equals moe_swiglu applied to moe_ep_run_compact's output. */
+int moe_ep_run_compact_swiglu(const moe_ep_run_params* params, int64_t send_rows, int64_t out_rows, void* stream);
+
 /* Copy the workspace status word to the host (synchronous). */
 int moe_ep_read_status(uint64_t local_base, const moe_ep_layout* layout, uint32_t* out);
 

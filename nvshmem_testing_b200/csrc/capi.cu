@@ -196,6 +196,16 @@ int moe_ep_run(const moe_ep_run_params* params, void* stream) {
   return launch_fused(params, FusedMode{}, static_cast<cudaStream_t>(stream));
 }
 
+int moe_ep_run_compact_swiglu(const moe_ep_run_params* params, int64_t send_rows, int64_t out_rows, void* stream) {
+  if (!params || send_rows < 0 || out_rows < 0) return kBadArg;
+  FusedMode m;
+  m.general = 1;
+  m.glu = 1;
+  m.send_rows = send_rows;
+  m.out_rows = out_rows;
+  return launch_fused(params, m, static_cast<cudaStream_t>(stream));
+}
+
 int moe_ep_run_compact(const moe_ep_run_params* params, int64_t send_rows, int64_t out_rows, void* stream) {
   if (!params || send_rows < 0 || out_rows < 0) return kBadArg;
   FusedMode m;

@@ -82,6 +82,7 @@ constexpr uint32_t kTmemCols = 2 * kAccCols;
 constexpr int kGoSlots = 8;                     // > kStages: the leader runs at most kStages k-blocks ahead
 constexpr int kRowMaps = 5;                     // B boxes of 8, 16, 32, 64, 128 rows
 constexpr int kNamedBarPush = 1;
+constexpr int kNamedBarEpi = 2;                 // the epilogue warps (SwiGLU mode)
 constexpr uint32_t kEpiStageBytes = kEpiWarps * 32 * 32 * 2;  // 32 rows x 32 features bf16 per warp
 
 struct Params {
@@ -110,6 +111,11 @@ struct Params {
   int general;
   int64_t send_rows, out_rows;
   int tile_cap;  // most rows per tile (multiple of 16, <= kMaxTileRows)
+  // SwiGLU mode (compact only): the weights hold, per 128 features of a CTA,
+  // 64 gate columns then the 64 matching up columns; the epilogue writes
+  // h = silu(gate) * up, N/2 columns per row.
+  int glu;
+  int out_cols;  // columns of an output row: N, or N/2 in SwiGLU mode
   int kstagger;  // tile t walks K from k-block t % kblocks (many tiles sharing one weight slice)
   int32_t* status_host;
   uint64_t* trace;  // MOE_EP_TRACE_WORDS per CTA, or null
@@ -685,35 +691,61 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tempty_leader = mapa_shared(smem_u32(&sm.tempty[0]), 0);
     uint32_t lt = 0;
     uint64_t epi_ns = 0;
+    // SwiGLU mode: quarters 0 and 1 hold gate features, 2 and 3 the matching
+    // up features; a gate warp reads its partner's staged values.  The four
+    // warps meet at named barriers, so they decide together whether to go on
+    // (bar.red.and) and never leave one of them waiting.
+    const __nv_bfloat16* partner =
+        reinterpret_cast<const __nv_bfloat16*>(epi_mem) + (quarter + 2 - (kWarpEpi0 & 3)) % 4 * 32 * 32;
     for (;; ++lt) {
-      const int t = wait_tile(sm, lt, pipe_bound);
+      int t = wait_tile(sm, lt, pipe_bound);
+      if (p.glu && !named_bar_and(kNamedBarEpi, kEpiWarps * 32, t >= 0)) t = -1;
       if (t < 0) break;
       const Tile tl = decode_tile(s, W, El, me, t);
       const uint32_t acc = lt & 1, use = lt >> 1;
       const uint64_t tp0 = TRACE_NOW(p);
-      if (!mbar_wait(&sm.tfull[acc], use & 1, pipe_bound, sm)) break;
+      bool full = mbar_wait(&sm.tfull[acc], use & 1, pipe_bound, sm);
+      if (p.glu) full = named_bar_and(kNamedBarEpi, kEpiWarps * 32, full);
+      if (!full) break;
       epi_ns += TRACE_NOW(p) - tp0;
       tc_fence_after();
-      const int fbase = tl.feat * kFeatPair + int(crank) * kFeatCta + quarter * 32;
+      const int fbase = p.glu ? tl.feat * (kFeatPair / 2) + int(crank) * (kFeatCta / 2) + quarter * 32
+                              : tl.feat * kFeatPair + int(crank) * kFeatCta + quarter * 32;
+      const bool stores = !p.glu || quarter < 2;
       for (int jc = 0; jc * 32 < tl.n; ++jc) {
         uint32_t r[32];
         __syncwarp();
         tmem_ld_32x32b_x32(tmem_base + acc * kAccCols + (uint32_t(quarter * 32) << 16) + jc * 32, r);
         tmem_ld_wait();
+        if (p.glu) named_bar_sync(kNamedBarEpi, kEpiWarps * 32);  // partners done with the last chunk
         // stage[i][lane] = D[feature fbase + lane][row jc*32 + i]
 #pragma unroll
         for (int i = 0; i < 32; ++i) stage[i * 32 + lane] = __float2bfloat16_rn(__uint_as_float(r[i]));
         __syncwarp();
+        if (p.glu) {
+          named_bar_sync(kNamedBarEpi, kEpiWarps * 32);  // every warp's chunk is staged
+          if (quarter < 2) {
+#pragma unroll 8
+            for (int i = 0; i < 32; ++i) {
+              const float g = __bfloat162float(stage[i * 32 + lane]);
+              const float u = __bfloat162float(partner[i * 32 + lane]);
+              stage[i * 32 + lane] = __float2bfloat16_rn((g / (1.f + expf(-g))) * u);
+            }
+            __syncwarp();
+          }
+        }
+        if (stores) {
 #pragma unroll
-        for (int step = 0; step < 4; ++step) {
-          const int c = lane + 32 * step;
-          const int i = c >> 2, part = c & 3;
-          const int row = tl.row0 + jc * 32 + i;
-          const int f = fbase + part * 8;
-          if (row < tl.row1 && f + 8 <= p.N) {
-            const uint4 v = *reinterpret_cast<const uint4*>(stage + i * 32 + part * 8);
-            if (p.ret) st_v4(ret_row_ptr(s, p, tl, row) + size_t(f) * 2, v);  // NVLink for remote rows
-            else *reinterpret_cast<uint4*>(p.out + out_row_of(s, p, tl, row) * p.N + f) = v;
+          for (int step = 0; step < 4; ++step) {
+            const int c = lane + 32 * step;
+            const int i = c >> 2, part = c & 3;
+            const int row = tl.row0 + jc * 32 + i;
+            const int f = fbase + part * 8;
+            if (row < tl.row1 && f + 8 <= p.out_cols) {
+              const uint4 v = *reinterpret_cast<const uint4*>(stage + i * 32 + part * 8);
+              if (p.ret) st_v4(ret_row_ptr(s, p, tl, row) + size_t(f) * 2, v);  // NVLink for remote rows
+              else *reinterpret_cast<uint4*>(p.out + out_row_of(s, p, tl, row) * p.out_cols + f) = v;
+            }
           }
         }
       }
@@ -983,6 +1015,7 @@ int launch_fused(const moe_ep_run_params* a, const FusedMode& m, cudaStream_t st
   if (ret && ret_rows < int64_t(W) * El * a->gm) return kBadArg;
   if (m.general && (ret || m.send_rows < 0 || m.out_rows < 0)) return kBadArg;
   if (m.tile_cap < 0 || m.tile_cap > kMaxTileRows || m.tile_cap % 16) return kBadArg;
+  if (m.glu && (!m.general || ret || a->out_dim % kFeatPair)) return kBadArg;
   if ((reinterpret_cast<uintptr_t>(a->tokens) | reinterpret_cast<uintptr_t>(a->weights) |
        reinterpret_cast<uintptr_t>(a->out)) & 15)
     return kBadArg;
@@ -1047,6 +1080,8 @@ int launch_fused(const moe_ep_run_params* a, const FusedMode& m, cudaStream_t st
   p.general = m.general;
   p.tile_cap = m.tile_cap > 0 ? m.tile_cap : kMaxTileRows;
   p.kstagger = m.kstagger;
+  p.glu = m.glu;
+  p.out_cols = m.glu ? a->out_dim / 2 : a->out_dim;
   p.send_rows = m.send_rows;
   p.out_rows = m.out_rows;
   p.status_host = a->status_host;

@@ -82,6 +82,7 @@ struct FusedMode {
   int64_t out_rows = 0;   // compact mode: rows of out
   int tile_cap = 0;       // most rows per GEMM tile (multiple of 16); 0 = 256
   int kstagger = 0;       // stagger each tile's first k-block (tiles that share weights)
+  int glu = 0;            // compact mode only: SwiGLU epilogue (out has out_dim / 2 columns)
 };
 int launch_fused(const moe_ep_run_params* a, const FusedMode& m, cudaStream_t stream);
 

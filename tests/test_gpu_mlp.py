@@ -82,6 +82,31 @@ def test_single_rank_mlp_matches_oracle(single_rank_group, El, H, F, counts):
     assert torch.equal(y, again)
 
 
+@pytest.mark.parametrize("El,H,F,counts", [c for c in CASES if c[2] % 128 == 0])
+def test_fused_swiglu_matches_separate_activation(single_rank_group, El, H, F, counts):
+    """The activation in the first GEMM's epilogue (moe_ep_run_compact_swiglu)
+    gives the values of the separate moe_swiglu pass: the same bf16 gate and
+    up values and the same fp32 arithmetic."""
+    g = torch.Generator().manual_seed(El * 7 + H + F)
+    total = sum(counts)
+    tok = torch.randn(total, H, generator=g).to(torch.bfloat16).cuda()
+    w13 = (0.05 * torch.randn(El, H, 2 * F, generator=g)).to(torch.bfloat16).cuda()
+    w2 = (0.05 * torch.randn(El, F, H, generator=g)).to(torch.bfloat16).cuda()
+    rc = torch.tensor([counts], dtype=torch.int32).cuda()
+    y_sep = mlp.run(0, tok, total, 1, w13, w2, rc, check=True)
+    w13f = mlp.fuse_gate_up(w13)
+    y_fused = mlp.run(0, tok, total, 1, w13f, w2, rc, check=True, w13_fused=True)
+    y_again = mlp.run(0, tok, total, 1, w13f, w2, rc, w13_fused=True)
+    torch.cuda.synchronize()
+    assert y_fused.shape == y_sep.shape
+    if total:
+        assert (y_fused == y_sep).float().mean().item() > 0.99
+        ref = oracle.mlp_compact([_f32(tok)], [np.array(counts)], [_f32(w13)], [_f32(w2)])[0]
+        errs = _errs(y_fused, ref)
+        assert not errs, errs
+    assert torch.equal(y_fused, y_again)
+
+
 def test_moe_mlp_from_routing(single_rank_group):
     wl = workloads.get("deepseek_v3", T=512, H=256, N=256, E=8)
     x = workloads.tokens(wl, 0).cuda()
@@ -117,9 +142,11 @@ def _worker(rank, world, port, q):
             w13s.append((0.05 * torch.randn(El, wl.H, 2 * F, generator=g)).to(torch.bfloat16))
             w2s.append((0.05 * torch.randn(El, F, wl.H, generator=g)).to(torch.bfloat16))
         errs = []
-        for k in range(2):
-            y, rc = mlp.moe_mlp(xs[rank].cuda(), ids[rank].cuda(), w13s[rank].cuda(), w2s[rank].cuda(),
-                                timeout_s=10.0)
+        for k in range(3):
+            w13 = w13s[rank].cuda()
+            fused = k == 2  # the third call with the activation in the GEMM epilogue
+            y, rc = mlp.moe_mlp(xs[rank].cuda(), ids[rank].cuda(), mlp.fuse_gate_up(w13) if fused else w13,
+                                w2s[rank].cuda(), timeout_s=10.0, w13_fused=fused)
             torch.cuda.synchronize()
             send, counts = [], []
             for r in range(world):
