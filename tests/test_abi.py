@@ -96,3 +96,20 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(N, "LIB_PATH", tmp_path / "absent.so")
     with pytest.raises(N.MoeEpError):
         N.lib()
+
+
+def test_fused_gate_up_layout():
+    """mlp.fuse_gate_up puts, per 256 columns, gate j..j+63, up j..j+63,
+    gate j+64..j+127, up j+64..j+127 (the SwiGLU epilogue's layout)."""
+    import torch
+    from nvshmem_testing_b200 import mlp
+    F = 256
+    w = torch.arange(2 * F, dtype=torch.float32).view(1, 1, 2 * F).expand(2, 3, 2 * F).contiguous()
+    got = mlp.fuse_gate_up(w)[1, 2].long().tolist()
+    want = []
+    for s in range(F // 128):
+        for c in range(2):
+            want += [s * 128 + c * 64 + j for j in range(64)] + [F + s * 128 + c * 64 + j for j in range(64)]
+    assert got == want
+    with pytest.raises(ValueError):
+        mlp.fuse_gate_up(torch.zeros(1, 4, 2 * 96))
