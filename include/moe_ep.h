@@ -15,11 +15,14 @@
  *                               signal buffers, rendezvous)
  *   moe_ep_workspace_layout     alltoall_persistent_gemm.py:187-195
  *                               (receive [W*transmit, H] + signal [W] shapes)
+ *   moe_ep_read_status          (status word; the reference has no error path)
+ *   moe_ep_run_noalloc          no counterpart (see its declaration)
  *   moe_ep_run                  alltoall_persistent_gemm.py:207-309 (run:
  *                               peer copies + flags + fused grouped GEMM) and
  *                               baseline.py:8-56 (same output contract)
- *   moe_swiglu                  the full expert MLP's activation (the
- *                               reference's expert is one GEMM, baseline.py:50)
+ *   moe_swiglu,                 the full expert MLP's activation, separate or
+ *   moe_ep_run_compact_swiglu   in the first GEMM's epilogue (the reference's
+ *                               expert is one GEMM, baseline.py:50)
  *   moe_router                  utils.py:17-25 (router logits einsum, softmax,
  *                               top-k: the step before the reference's path)
  *   moe_pack_compact,           the general (unbalanced) all-to-all that
