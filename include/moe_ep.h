@@ -54,7 +54,7 @@ extern "C" {
 #define MOE_EP_CAPACITY 4
 #define MOE_EP_BAD_ROUTE 5
 
-#define MOE_EP_ABI_VERSION 2
+#define MOE_EP_ABI_VERSION 3
 
 int moe_ep_abi_version(void);
 const char* moe_ep_status_string(int code);
@@ -177,6 +177,17 @@ typedef struct moe_ep_run_params {
   int32_t* status_host;        /* optional mapped pinned word for device errors      */
   uint64_t* trace;             /* optional device timeline, MOE_EP_TRACE_WORDS per  */
                                /* CTA (NULL = off); see MOE_EP_TRACE_* below         */
+  int32_t push_ctas;           /* CTAs (even, at the end of the grid) that only     */
+                               /* move rows to peers and zero padded rows, with all */
+                               /* their warps; 0 = two push warps in every CTA      */
+  int32_t local_first;         /* experts whose local tiles all run before any      */
+                               /* remote tile (0 = expert-major order throughout)   */
+  int32_t counts_are_send;     /* 1: recv_counts holds this rank's SEND counts      */
+                               /* [W dst, El] (the routing's per-expert counts)     */
+                               /* instead of its receive counts; the kernel's own   */
+                               /* count exchange then replaces the host-side count  */
+                               /* all-to-all of benchmark.py:114-118                */
+  int32_t reserved0;           /* 0                                                 */
 } moe_ep_run_params;
 
 /* Device timeline (globaltimer ns, or counts), one record per CTA. */
@@ -230,11 +241,16 @@ int moe_ep_run_compact(const moe_ep_run_params* params, int64_t send_rows, int64
  * cap_rows, push_rows, max_chunks and epoch are ignored.  More than
  * MOE_EP_NOALLOC_MAX_EXPERTS local experts returns MOE_EP_SCRATCH_LIMIT.
  * Allocates nothing: no cudaMalloc/cudaFree, no allocating library call.
- * The first call on a device looks up the array's address and writes it
- * synchronously, so make that call before any stream capture.  Every call
- * reuses the same array and clears its control words first, so calls whose
+ * The first call on a device looks up the array's address (a host-side
+ * lookup), so make that call before any stream capture; every call then
+ * prepares the array in stream order (a one-block kernel writes the one-entry
+ * peer table and clears the control words the previous call left) and
+ * launches the layer.  Every call reuses the same array, so calls whose
  * kernels overlap on the GPU (different streams, or several threads) race and
- * must not be made; errors are reported through status_host. */
+ * must not be made; calls queued on one stream are fine.  Device-side errors
+ * (a count above gm, a timed-out wait) are reported only through the mapped
+ * pinned word status_host, which is therefore required (NULL returns
+ * MOE_EP_BAD_ARG); the caller clears it between calls. */
 #define MOE_EP_SCRATCH_LIMIT 6
 #define MOE_EP_NOALLOC_MAX_EXPERTS 64
 #define MOE_EP_NOALLOC_SCRATCH_BYTES 2048

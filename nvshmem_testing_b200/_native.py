@@ -17,7 +17,7 @@ STATUS_NAMES = {OK: "ok", BAD_ARG: "bad argument", CUDA_ERR: "CUDA error", TIMEO
                 CAPACITY: "receive capacity exceeded", BAD_ROUTE: "bad routing input",
                 SCRATCH_LIMIT: "size exceeds the fixed scratch of moe_ep_run_noalloc"}
 NOALLOC_MAX_EXPERTS = 64
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 # Every symbol include/moe_ep.h declares.
 EXPORTED = ["moe_ep_abi_version", "moe_ep_status_string", "moe_ep_num_sms", "moe_route", "moe_pack_padded",
@@ -50,7 +50,9 @@ class RunParams(ctypes.Structure):
                 ("recv_counts", ctypes.c_void_p), ("out", ctypes.c_void_p), ("peer_bases", ctypes.c_void_p),
                 ("local_base", ctypes.c_uint64), ("cap_rows", ctypes.c_int64), ("push_rows", ctypes.c_int32),
                 ("max_chunks", ctypes.c_int32), ("epoch", ctypes.c_uint32), ("num_ctas", ctypes.c_uint32),
-                ("timeout_ns", ctypes.c_uint64), ("status_host", ctypes.c_void_p), ("trace", ctypes.c_void_p)]
+                ("timeout_ns", ctypes.c_uint64), ("status_host", ctypes.c_void_p), ("trace", ctypes.c_void_p),
+                ("push_ctas", ctypes.c_int32), ("local_first", ctypes.c_int32),
+                ("counts_are_send", ctypes.c_int32), ("reserved0", ctypes.c_int32)]
 
 
 class CombineParams(ctypes.Structure):

@@ -40,6 +40,23 @@ from .symm import get_workspace
 
 DEFAULT_PUSH_ROWS = int(os.environ.get("MOE_EP_PUSH_ROWS", "32"))
 DEFAULT_TIMEOUT_S = float(os.environ.get("MOE_EP_TIMEOUT_S", "20"))
+# Dispatch placement with more than one rank: CTAs that only push rows (0 =
+# two push warps in every CTA), and experts whose local tiles run first.
+DEFAULT_PUSH_CTAS = int(os.environ.get("MOE_EP_PUSH_CTAS", "0"))
+DEFAULT_LOCAL_FIRST = int(os.environ.get("MOE_EP_LOCAL_FIRST", "0"))
+
+
+def placement(W: int, El: int, push_ctas: int | None = None, local_first: int | None = None) -> tuple[int, int]:
+    """(push_ctas, local_first) for a launch: one rank has no rows to push
+    and no remote tiles, so both are 0 there; otherwise the given values or
+    the defaults, local_first clamped to the local experts."""
+    if W == 1:
+        return 0, 0
+    pc = DEFAULT_PUSH_CTAS if push_ctas is None else int(push_ctas)
+    lf = DEFAULT_LOCAL_FIRST if local_first is None else int(local_first)
+    if pc < 0 or pc % 2:
+        raise ValueError(f"push_ctas must be even and >= 0, got {pc}")
+    return pc, max(0, min(lf, El))
 
 
 def _group_info(group, world_size: int, rank: int) -> tuple[int, int]:
@@ -58,7 +75,8 @@ def raise_if_device_error(ws) -> None:
 
 def _launch_params(me: int, W: int, tokens: torch.Tensor, gm: int | None, transmit_size: int, hidden_dim: int,
                    local_weights: torch.Tensor, recv_counts, group, timeout_s, push_rows, num_ctas, trace,
-                   ret_cols: int = 0):
+                   ret_cols: int = 0, push_ctas: int | None = None, local_first: int | None = None,
+                   send_counts: torch.Tensor | None = None):
     """Validate the fused layer's inputs and fill ``moe_ep_run_params``.
 
     ``gm`` is the bound on every (rank, expert) count; ``None`` means the
@@ -81,7 +99,13 @@ def _launch_params(me: int, W: int, tokens: torch.Tensor, gm: int | None, transm
     dev = tokens.device.index if tokens.device.index is not None else torch.cuda.current_device()
     tokens = tokens.contiguous()
     local_weights = local_weights.contiguous()
-    if recv_counts is None:
+    if send_counts is not None:
+        # This rank's per-expert send counts; the kernel's count exchange
+        # gives every rank the whole matrix.
+        if send_counts.numel() != W * El:
+            raise ValueError(f"send_counts must hold {W}x{El} counts, got {tuple(send_counts.shape)}")
+        recv_counts = send_counts.to(device=tokens.device, dtype=torch.int32).reshape(W, El).contiguous()
+    elif recv_counts is None:
         recv_counts = torch.full((W, El), gm, dtype=torch.int32, device=tokens.device)
     else:
         if tuple(recv_counts.shape) != (W, El):
@@ -101,6 +125,8 @@ def _launch_params(me: int, W: int, tokens: torch.Tensor, gm: int | None, transm
     p.cap_rows, p.push_rows, p.max_chunks = ws.key.cap_rows, ws.push_rows, ws.key.max_chunks
     p.epoch = ws.next_epoch()
     p.num_ctas = num_ctas
+    p.push_ctas, p.local_first = placement(W, El, push_ctas, local_first)
+    p.counts_are_send = int(send_counts is not None)
     p.timeout_ns = int((timeout_s if timeout_s is not None else DEFAULT_TIMEOUT_S) * 1e9)
     p.status_host = ws.status_host.data_ptr()
     if trace is not None:
@@ -128,7 +154,8 @@ def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: in
         local_weights: torch.Tensor = None, recv_counts: torch.Tensor = None, *, group=None,
         timeout_s: float | None = None, push_rows: int | None = None, num_ctas: int = 0,
         check: bool = False, trace: torch.Tensor | None = None, max_count: int | None = None,
-        recv_rows: int | None = None) -> torch.Tensor:
+        recv_rows: int | None = None, push_ctas: int | None = None, local_first: int | None = None,
+        send_counts: torch.Tensor | None = None) -> torch.Tensor:
     """Fused dispatch + grouped GEMM; see the module docstring.
 
     ``general_a2a=True`` (a stub in the reference, alltoall_persistent_gemm.py:221-222)
@@ -148,13 +175,20 @@ def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: in
     (rows per NVLink chunk and arrival flag), ``num_ctas`` (0 = one per SM),
     ``check`` (synchronise and raise on a device error before returning),
     ``trace`` (int64 device tensor of at least ``num_sms * 24`` words that
-    receives the per-CTA device timeline, ``_native.TRACE_FIELDS``).
+    receives the per-CTA device timeline, ``_native.TRACE_FIELDS``),
+    ``push_ctas`` / ``local_first`` (dispatch placement, see ``placement``),
+    ``send_counts`` (padded path only: this rank's ``[W*El]`` per-expert
+    counts, i.e. the routing's ``lengths``, in place of ``recv_counts``; the
+    kernel's count exchange then replaces the count all-to-all of
+    benchmark.py:114-118, so no collective or host read precedes the call).
     """
     assert dist.is_initialized()
     assert tokens.is_cuda
     me, W = _group_info(group, world_size, rank)
     if W != world_size or me != rank:
         raise ValueError(f"rank/world_size ({rank}/{world_size}) disagree with the process group ({me}/{W})")
+    if send_counts is not None and (general_a2a or recv_counts is not None):
+        raise ValueError("send_counts replaces recv_counts and needs the padded layout (general_a2a=False)")
     if general_a2a:
         if recv_counts is None:
             raise ValueError("general_a2a needs recv_counts [W, El]")
@@ -168,7 +202,8 @@ def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: in
         if send_rows == 0:  # nothing to send: any valid 16-byte-aligned row serves as the (unread) buffer
             tokens = torch.zeros((1, tokens.shape[1]), dtype=tokens.dtype, device=tokens.device)
         ws, p, (El, gm, Nout), keep = _launch_params(me, W, tokens, gm, transmit_size, hidden_dim, local_weights,
-                                                     recv_counts, group, timeout_s, push_rows, num_ctas, trace)
+                                                     recv_counts, group, timeout_s, push_rows, num_ctas, trace,
+                                                     push_ctas=push_ctas, local_first=local_first)
         # A zero-row view has a null data_ptr; the kernel wants a real buffer.
         buf = torch.empty((max(out_rows, 1), Nout), dtype=torch.bfloat16, device=tokens.device)
         out = buf[:out_rows]
@@ -179,7 +214,9 @@ def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: in
     else:
         assert tokens.shape[0] == transmit_size * world_size
         ws, p, (El, gm, Nout), keep = _launch_params(me, W, tokens, None, transmit_size, hidden_dim, local_weights,
-                                                     recv_counts, group, timeout_s, push_rows, num_ctas, trace)
+                                                     recv_counts, group, timeout_s, push_rows, num_ctas, trace,
+                                                     push_ctas=push_ctas, local_first=local_first,
+                                                     send_counts=send_counts)
         out = torch.empty((El, W * gm, Nout), dtype=torch.bfloat16, device=tokens.device)
         p.out = out.data_ptr()
         stream = torch.cuda.current_stream(tokens.device)
@@ -188,3 +225,29 @@ def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: in
         stream.synchronize()
         raise_if_device_error(ws)
     return out
+
+
+def layer(tokens: torch.Tensor, top_idxs: torch.Tensor, num_experts: int, local_weights: torch.Tensor, *,
+          group=None, gm: int | None = None, **kw) -> torch.Tensor:
+    """The whole path from token rows and routing ids: device routing
+    (utils.py:28-41), the padded expert-major send buffer (utils.py:45-69)
+    and the fused exchange + grouped GEMM (``run``), returning
+    ``[El, W*gm, N]`` like ``run``.
+
+    The only host read is the group's largest bucket, ``gm`` (an all-reduced
+    MAX of the device routing's local maxima; it sizes the padded buffers, as
+    ``chunk_size`` does in the reference); pass ``gm`` to skip it.  Counts
+    are not exchanged on the host: ``run`` receives this rank's send counts
+    and exchanges them inside the kernel.  Keyword arguments go to ``run``.
+    """
+    from . import utils
+    me, W = _group_info(group, 1, 0)
+    if num_experts % W:
+        raise ValueError(f"{num_experts} experts do not split over {W} ranks")
+    El = num_experts // W
+    r = utils.route(top_idxs, num_experts)
+    g = utils.global_max_count(r, group) if gm is None else max(int(gm), 1)
+    coalesced = utils.pack_padded(tokens, r, g)
+    T = int(top_idxs.shape[0])
+    return run(me, coalesced, El * g, 1, T, tokens.shape[1], num_experts, W, None, False, local_weights, None,
+               group=group, send_counts=r.counts, **kw)

@@ -117,6 +117,18 @@ struct Params {
   int glu;
   int out_cols;  // columns of an output row: N, or N/2 in SwiGLU mode
   int kstagger;  // tile t walks K from k-block t % kblocks (many tiles sharing one weight slice)
+  // Dispatch placement: the last push_ctas CTAs of the grid (whole clusters)
+  // only move rows to peers and zero padded rows, with all their warps; the
+  // others only compute.  0: two push warps in every CTA.
+  int push_ctas;
+  // Tile order: the local tiles of experts [0, local_first) come before any
+  // remote tile, so the GEMM starts on rows that need no NVLink transfer.
+  int local_first;
+  // recv_counts holds this rank's send counts [W dst][El] instead of its
+  // receive counts [W src][El]; every rank publishes its block either way,
+  // so the exchanged matrix is read transposed and no host-side count
+  // all-to-all is needed.
+  int send_counts;
   int32_t* status_host;
   uint64_t* trace;  // MOE_EP_TRACE_WORDS per CTA, or null
 };
@@ -143,7 +155,8 @@ struct Sched {
   int push_off[kMaxCells];                // [d][le] first destination row at rank d
   int push_cnt[kMaxCells];                // [d][le] rows this rank sends to (d, le)
   int push_pfx[kMaxCells + 1];            // prefix of push items over cells le*(W-1) + (q-1)
-  int tile_pfx[kMaxLocalExperts + 1];     // prefix of tiles over experts
+  int tile_pfx[kMaxLocalExperts + 1];     // prefix of tiles over experts (after the local-first tiles)
+  int lf_pfx[kMaxLocalExperts + 1];       // prefix of the local-first tiles over experts [0, local_first)
   int loc_nt[kMaxLocalExperts];           // local row tiles of expert le
   int rem_nt[kMaxLocalExperts];           // remote row tiles of expert le
   int tmp[kMaxCells];                     // scratch while building
@@ -252,17 +265,29 @@ struct Tile {
 // Tiles are expert-major: expert le's cell holds nfeat feature slices, each
 // followed by all of its row tiles (local first, then remote), so the tiles
 // that share a weight slice run back to back on neighbouring clusters and
-// read it once from HBM.
-__device__ __forceinline__ Tile decode_tile(const Sched& s, int W, int El, int me, int t) {
-  const int c = find_cell(s.tile_pfx, El, t);
-  const int r = t - s.tile_pfx[c];
-  const int nrt = s.loc_nt[c] + s.rem_nt[c];
+// read it once from HBM.  With local_first = X > 0 the local tiles of
+// experts [0, X) come first of all (same order among themselves), and those
+// experts' cells then hold only their remote tiles.
+__device__ __forceinline__ Tile decode_tile(const Sched& s, int W, int El, int me, int lf, int t) {
+  const int lf_total = s.lf_pfx[lf];
+  int c, r, lnt, nrt;
+  if (t < lf_total) {
+    c = find_cell(s.lf_pfx, lf, t);
+    r = t - s.lf_pfx[c];
+    lnt = nrt = s.loc_nt[c];
+  } else {
+    t -= lf_total;
+    c = find_cell(s.tile_pfx, El, t);
+    r = t - s.tile_pfx[c];
+    lnt = c < lf ? 0 : s.loc_nt[c];
+    nrt = lnt + s.rem_nt[c];
+  }
   Tile tl;
   tl.le = c;
   tl.feat = r / nrt;
   int i = r % nrt;
-  tl.remote = i >= s.loc_nt[c];
-  if (tl.remote) i -= s.loc_nt[c];
+  tl.remote = i >= lnt;
+  if (tl.remote) i -= lnt;
   const int rows = tl.remote ? s.seg[tl.le * (W + 1) + W] : s.cnt[me * El + tl.le];
   const int tr = tl.remote ? s.rem_tr[tl.le] : s.loc_tr[tl.le];
   tl.row0 = i * tr;
@@ -309,8 +334,13 @@ __device__ void build_schedule(const Params& p, Sched& s, Smem& sm) {
   // One rank reads its own recv_counts (nothing was exchanged).
   const int32_t* cm = W == 1 ? p.recv_counts
                              : reinterpret_cast<const int32_t*>(p.local + p.off_cmat) + size_t(par) * W * W * El;
-  // cmat[owner][src][le]: rows src sends to owner's local expert le.
-  auto C = [&](int owner, int src, int le) { return cm[(size_t(owner) * W + src) * El + le]; };
+  // C(owner, src, le): rows src sends to owner's local expert le.  The
+  // matrix holds every rank's published block: receive counts (block =
+  // owner) or send counts (block = src).
+  const bool by_src = p.send_counts != 0;
+  auto C = [&](int owner, int src, int le) {
+    return by_src ? cm[(size_t(src) * W + owner) * El + le] : cm[(size_t(owner) * W + src) * El + le];
+  };
   const int nfeat = (p.N + kFeatPair - 1) / kFeatPair;
 
   if (tid == 0) {
@@ -365,7 +395,9 @@ __device__ void build_schedule(const Params& p, Sched& s, Smem& sm) {
     s.loc_nt[le] = (lr + s.loc_tr[le] - 1) / s.loc_tr[le];
     s.rem_nt[le] = (run + s.rem_tr[le] - 1) / s.rem_tr[le];
     s.rbase[le] = run;                                   // scanned below
-    s.tile_pfx[le] = (s.loc_nt[le] + s.rem_nt[le]) * nfeat;  // scanned below
+    const bool lf = le < p.local_first;
+    s.tile_pfx[le] = ((lf ? 0 : s.loc_nt[le]) + s.rem_nt[le]) * nfeat;  // scanned below
+    s.lf_pfx[le] = lf ? s.loc_nt[le] * nfeat : 0;                     // scanned below
   }
   __syncthreads();
 
@@ -387,7 +419,8 @@ __device__ void build_schedule(const Params& p, Sched& s, Smem& sm) {
   }
   if (warp == 1) {
     warp_exclusive_scan(s.tile_pfx, El, lane);
-    if (lane == 0) s.tiles_total = s.tile_pfx[El];
+    warp_exclusive_scan(s.lf_pfx, p.local_first, lane);
+    if (lane == 0) s.tiles_total = s.tile_pfx[El] + s.lf_pfx[p.local_first];
     if (p.general) {
       warp_exclusive_scan(s.ooff, W * El, lane);
       if (lane == 0 && int64_t(s.ooff[W * El]) > p.out_rows) raise_error(p, sm, kBadArg, kSiteTable, 0xFFFF);
@@ -442,6 +475,21 @@ __device__ __forceinline__ unsigned char* ret_row_ptr(const Sched& s, const Para
          ((int64_t(p.me) * p.El + tl.le) * p.gm + i) * int64_t(p.N) * 2;
 }
 
+// One push item's rows: nvec 16-byte vectors from this GPU's send buffer to
+// a peer's receive region, U loads in flight per thread before their stores.
+template <int U>
+__device__ __forceinline__ void copy_rows(const uint4* src, uint4* dst, int64_t nvec, int pt, int np) {
+  int64_t v = pt;
+  for (; v + (U - 1) * np < nvec; v += U * np) {
+    uint4 a[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) a[u] = ld_nc_v4(src + v + u * np);
+#pragma unroll
+    for (int u = 0; u < U; ++u) st_v4(dst + v + u * np, a[u]);
+  }
+  for (; v < nvec; v += np) st_v4(dst + v, ld_nc_v4(src + v));
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     fused_ep_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_w4,
                     const __grid_constant__ RowMaps rows_local,
@@ -458,6 +506,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t par = p.epoch & 1u;
   const uint32_t crank = cluster_ctarank();
   const bool leader = crank == 0;
+  // Whole clusters at the end of the grid only push (see Params::push_ctas).
+  const bool push_cta = p.push_ctas > 0 && int(blockIdx.x) >= int(gridDim.x) - p.push_ctas;
   const uint64_t pipe_bound = 2 * p.timeout_ns + 1000000000ull;
   LocalWords* lw = reinterpret_cast<LocalWords*>(p.local + p.off_local);
   if (tid == 0) TRACE_SET(p, MOE_EP_TRACE_START, TRACE_NOW(p));
@@ -483,7 +533,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tensormap(&tm_w);
   }
   cluster_sync();  // the peer's barriers exist before any remote arrive
-  if (warp == kWarpMma) {
+  if (warp == kWarpMma && !push_cta) {
     __syncwarp();
     tmem_alloc_pair(&sm.tmem_base, kTmemCols);
     tmem_relinquish_pair();
@@ -534,7 +584,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool run_main = !aborted(sm);
   if (tid == 0) TRACE_SET(p, MOE_EP_TRACE_SCHED, TRACE_NOW(p));
 
-  if (run_main && warp == kWarpProducer) {
+  // Rows are pushed by two warps of every CTA, or by every warp of the push
+  // CTAs; the other warps of push CTAs have no role.
+  const bool pusher = push_cta || (p.push_ctas == 0 && warp >= kWarpPush0);
+  if (run_main && !push_cta && warp == kWarpProducer) {
     if (lane == 0) {
       const uint32_t bar_leader0 = mapa_shared(smem_u32(&sm.full[0]), 0);
       uint32_t it = 0, ti = 0;
@@ -550,7 +603,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           t = (aborted(sm) || claimed >= s.tiles_total) ? -1 : claimed;
           if (t >= 0) claimed = int(atomicAdd(&lw->tile_ctr[par], 1u));
           bool ok = t >= 0;
-          if (ok) tl = decode_tile(s, W, El, me, t);
+          if (ok) tl = decode_tile(s, W, El, me, p.local_first, t);
           const uint64_t tw0 = TRACE_NOW(p);
           if (ok && tl.remote) {
             const int* sg = s.seg + tl.le * (W + 1);
@@ -578,7 +631,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
           t = wait_tile(sm, ti, pipe_bound);
           if (t < 0) break;
-          tl = decode_tile(s, W, El, me, t);
+          tl = decode_tile(s, W, El, me, p.local_first, t);
         }
         if (tl.remote) fence_proxy_async_global();
         const int half = tl.n >> 1;
@@ -636,14 +689,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       TRACE_SET(p, MOE_EP_TRACE_FLAG_WAIT, flag_ns);
       TRACE_SET(p, MOE_EP_TRACE_EMPTY_WAIT, empty_ns);
     }
-  } else if (run_main && warp == kWarpMma) {
+  } else if (run_main && !push_cta && warp == kWarpMma) {
     if (leader && lane == 0) {
       uint32_t it = 0, lt = 0;
       uint64_t full_ns = 0, acc_ns = 0, issue_ns = 0;
       for (;; ++lt) {
         const int t = wait_tile(sm, lt, pipe_bound);
         if (t < 0) break;
-        const Tile tl = decode_tile(s, W, El, me, t);
+        const Tile tl = decode_tile(s, W, El, me, p.local_first, t);
         const uint32_t acc = lt & 1, use = lt >> 1;
         const uint64_t ta0 = TRACE_NOW(p);
         if (!mbar_wait(&sm.tempty[acc], (use & 1) ^ 1, pipe_bound, sm, true)) break;
@@ -685,7 +738,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       TRACE_SET(p, MOE_EP_TRACE_MMA_ISSUE, issue_ns);
       TRACE_SET(p, MOE_EP_TRACE_KBLOCKS, it);
     }
-  } else if (run_main && warp >= kWarpEpi0 && warp < kWarpPush0) {
+  } else if (run_main && !push_cta && warp >= kWarpEpi0 && warp < kWarpPush0) {
     const int quarter = warp & 3;
     __nv_bfloat16* stage = reinterpret_cast<__nv_bfloat16*>(epi_mem) + (warp - kWarpEpi0) * 32 * 32;
     const uint32_t tempty_leader = mapa_shared(smem_u32(&sm.tempty[0]), 0);
@@ -701,7 +754,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int t = wait_tile(sm, lt, pipe_bound);
       if (p.glu && !named_bar_and(kNamedBarEpi, kEpiWarps * 32, t >= 0)) t = -1;
       if (t < 0) break;
-      const Tile tl = decode_tile(s, W, El, me, t);
+      const Tile tl = decode_tile(s, W, El, me, p.local_first, t);
       const uint32_t acc = lt & 1, use = lt >> 1;
       const uint64_t tp0 = TRACE_NOW(p);
       bool full = mbar_wait(&sm.tfull[acc], use & 1, pipe_bound, sm);
@@ -758,8 +811,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       TRACE_SET(p, MOE_EP_TRACE_EPI_END, TRACE_NOW(p));
       TRACE_SET(p, MOE_EP_TRACE_EPI_WAIT, epi_ns);
     }
-  } else if (run_main && warp >= kWarpPush0) {
-    const int pt = tid - kWarpPush0 * 32;
+  } else if (run_main && pusher) {
+    const int np = push_cta ? kThreads : kPushThreads;  // threads taking part in each item
+    const int pt = push_cta ? tid : tid - kWarpPush0 * 32;
     const size_t row_bytes = size_t(p.H) * 2;
     uint64_t items = 0, bytes = 0;
     bool pushes_done = false;
@@ -776,9 +830,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         sm.push_item = it;
       }
-      named_bar_sync(kNamedBarPush, kPushThreads);
+      named_bar_sync(kNamedBarPush, np);
       const int item = sm.push_item;
-      named_bar_sync(kNamedBarPush, kPushThreads);
+      named_bar_sync(kNamedBarPush, np);
       if (item < s.push_total) {
         const int c = find_cell(s.push_pfx, (W - 1) * El, item);
         const int q = c % (W - 1) + 1, le = c / (W - 1);
@@ -792,20 +846,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint4* dst = reinterpret_cast<uint4*>(peer + p.off_data +
                                               (size_t(par) * p.cap_rows + s.push_off[d * El + le] + j0) * row_bytes);
         const int64_t nvec = int64_t(j1 - j0) * int64_t(row_bytes / 16);
-        int64_t v = pt;
-        for (; v + 3 * kPushThreads < nvec; v += 4 * kPushThreads) {
-          const uint4 a0 = ld_nc_v4(src + v);
-          const uint4 a1 = ld_nc_v4(src + v + kPushThreads);
-          const uint4 a2 = ld_nc_v4(src + v + 2 * kPushThreads);
-          const uint4 a3 = ld_nc_v4(src + v + 3 * kPushThreads);
-          st_v4(dst + v, a0);
-          st_v4(dst + v + kPushThreads, a1);
-          st_v4(dst + v + 2 * kPushThreads, a2);
-          st_v4(dst + v + 3 * kPushThreads, a3);
-        }
-        for (; v < nvec; v += kPushThreads) st_v4(dst + v, ld_nc_v4(src + v));
+        // More loads in flight per thread where a whole CTA pushes: the copy
+        // is bound by bytes in flight over the local load latency.
+        if (push_cta) copy_rows<16>(src, dst, nvec, pt, np);
+        else copy_rows<4>(src, dst, nvec, pt, np);
         fence_acq_rel_sys();
-        named_bar_sync(kNamedBarPush, kPushThreads);
+        named_bar_sync(kNamedBarPush, np);
         if (pt == 0) {
           uint32_t* fl = at_u32(peer, p.off_dflag) + ((size_t(par) * W + me) * El + le) * p.max_chunks + chunk;
           st_release_sys(fl, p.epoch);
@@ -823,7 +869,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int64_t nvec = (p.gm - c0) * int64_t(p.N) / 8;
         uint4* dst = reinterpret_cast<uint4*>(p.out + (int64_t(le) * W * p.gm + int64_t(src) * p.gm + c0) * p.N);
         const uint4 zv = make_uint4(0, 0, 0, 0);
-        for (int64_t v = pt; v < nvec; v += kPushThreads) dst[v] = zv;
+        for (int64_t v = pt; v < nvec; v += np) dst[v] = zv;
       } else {
         break;
       }
@@ -861,7 +907,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   }
-  if (leader && warp == kWarpMma && lane == 0) {
+  if (leader && !push_cta && warp == kWarpMma && lane == 0) {
     tc_commit_pair(&sm.drain);
     const uint64_t deadline = globaltimer_ns() + 1000000000ull;
     while (!mbar_try_wait(&sm.drain, 0)) {
@@ -874,7 +920,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   cluster_sync();
   tc_fence_after();
-  if (warp == kWarpMma) {
+  if (warp == kWarpMma && !push_cta) {
     __syncwarp();
     tmem_dealloc_pair(tmem_base, kTmemCols);
   }
@@ -1020,6 +1066,7 @@ int launch_fused(const moe_ep_run_params* a, const FusedMode& m, cudaStream_t st
        reinterpret_cast<uintptr_t>(a->out)) & 15)
     return kBadArg;
   if (a->num_ctas & 1u) return kBadArg;  // CTA pairs
+  if (a->push_ctas < 0 || (a->push_ctas & 1) || a->local_first < 0 || a->local_first > El) return kBadArg;
   // Rows of the token buffer (the local TMA map's extent).
   const int64_t rows_in = m.general ? m.send_rows : int64_t(W) * El * a->gm;
   if (rows_in + kMaxTileRows > (int64_t(1) << 31) || 2 * a->cap_rows + kMaxTileRows > (int64_t(1) << 31) ||
@@ -1086,6 +1133,9 @@ int launch_fused(const moe_ep_run_params* a, const FusedMode& m, cudaStream_t st
   p.out_rows = m.out_rows;
   p.status_host = a->status_host;
   p.trace = a->trace;
+  p.push_ctas = a->push_ctas;
+  p.local_first = a->local_first;
+  p.send_counts = a->counts_are_send != 0;
 
   const size_t smem = fused_smem_bytes();
   int dev = 0;
@@ -1116,6 +1166,7 @@ int launch_fused(const moe_ep_run_params* a, const FusedMode& m, cudaStream_t st
     info.ready = true;
   }
   const int grid = a->num_ctas > 0 ? int(a->num_ctas) : info.grid;
+  if (a->push_ctas > grid - 2) return kBadArg;  // at least one computing pair
   cfg.gridDim = dim3(unsigned(grid), 1, 1);
   if (cudaLaunchKernelEx(&cfg, fused_ep_kernel, tw, tw4, rl, rr, p) != cudaSuccess) return kCudaErr;
   return cudaGetLastError() == cudaSuccess ? kOk : kCudaErr;

@@ -15,8 +15,9 @@
 // library holds a copy until the process exits.  Host code cannot use its
 // name as a device address, so the first call on each device looks the
 // address up with cudaGetSymbolAddress (with that device current) and
-// records it; that first call also writes the one-entry peer table and is
-// synchronous, so it should happen before any stream capture.
+// records it; make that first call before any stream capture.  Every call
+// then prepares the array in stream order with a one-block kernel (the
+// one-entry peer table and zeroed control words) before the layer kernel.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -39,21 +40,25 @@ __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 uint64_t g_scratch_addr[kMaxDevices];  // device address of the array per device; 0 = not yet looked up
 std::mutex g_setup;
 
-// Once per device, with `dev` current: find the array's device address and
-// store the control base in its peer-table slot.
+// Once per device, with `dev` current: the array's device address.
 int scratch_address(int dev, uint64_t* out) {
   std::lock_guard<std::mutex> lock(g_setup);
   if (g_scratch_addr[dev] == 0) {
     void* ptr = nullptr;
     if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) return kCudaErr;
-    const uint64_t control_base = reinterpret_cast<uint64_t>(ptr) + kPeerTableBytes;
-    if (cudaMemcpyToSymbol(g_noalloc_scratch, &control_base, sizeof(control_base), 0, cudaMemcpyHostToDevice) !=
-        cudaSuccess)
-      return kCudaErr;
     g_scratch_addr[dev] = reinterpret_cast<uint64_t>(ptr);
   }
   *out = g_scratch_addr[dev];
   return kOk;
+}
+
+// In stream order before each layer kernel: the peer-table slot holds the
+// control base, and the control words the previous call left start at zero.
+__global__ void prepare_scratch_kernel(uint32_t ctrl_words) {
+  if (threadIdx.x == 0)
+    *reinterpret_cast<uint64_t*>(g_noalloc_scratch) = reinterpret_cast<uint64_t>(g_noalloc_scratch + kPeerTableBytes);
+  uint32_t* ctrl = reinterpret_cast<uint32_t*>(g_noalloc_scratch + kPeerTableBytes);
+  for (uint32_t i = threadIdx.x; i < ctrl_words; i += blockDim.x) ctrl[i] = 0u;
 }
 
 }  // namespace
@@ -62,6 +67,9 @@ extern "C" int moe_ep_run_noalloc(const moe_ep_run_params* params, void* stream)
   if (!params) return kBadArg;
   if (params->world_size != 1 || params->rank != 0 || params->local_experts < 1) return kBadArg;
   if (params->local_experts > MOE_EP_NOALLOC_MAX_EXPERTS) return MOE_EP_SCRATCH_LIMIT;
+  // The control words are cleared by the next call, so a device-side error
+  // can only be read through the caller's mapped status word: require it.
+  if (!params->status_host) return kBadArg;
   if (params->gm < 0 || params->gm > (int64_t(1) << 30)) return kBadArg;
 
   // One flag slot per expert: a chunk of gm rows covers every valid count.
@@ -79,8 +87,8 @@ extern "C" int moe_ep_run_noalloc(const moe_ep_run_params* params, void* stream)
   // The array keeps whatever the previous call left there; the kernel needs
   // zeroed counters and epochs, so clear the control region in stream order.
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (cudaMemsetAsync(reinterpret_cast<void*>(scratch + kPeerTableBytes), 0, L.ctrl_bytes, s) != cudaSuccess)
-    return kCudaErr;
+  prepare_scratch_kernel<<<1, 256, 0, s>>>(uint32_t(L.ctrl_bytes / 4));
+  if (cudaGetLastError() != cudaSuccess) return kCudaErr;
 
   moe_ep_run_params q = *params;
   q.peer_bases = reinterpret_cast<const uint64_t*>(scratch);
@@ -89,5 +97,7 @@ extern "C" int moe_ep_run_noalloc(const moe_ep_run_params* params, void* stream)
   q.push_rows = push_rows;
   q.max_chunks = 1;
   q.epoch = 1;
+  q.push_ctas = 0;
+  q.local_first = 0;
   return launch_fused(&q, FusedMode{}, s);
 }

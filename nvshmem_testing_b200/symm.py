@@ -106,6 +106,10 @@ class WorkspaceKey:
     ret_cols: int = 0
 
 
+# Largest epoch a launch may carry (the device word is 32 bits).
+EPOCH_LIMIT = 2**32 - 1
+
+
 class SymmetricWorkspace:
     """One rank's mapped view of all ranks' workspaces."""
 
@@ -167,8 +171,33 @@ class SymmetricWorkspace:
             _barrier(group)  # every rank has zeroed and mapped before the first call
 
     def next_epoch(self) -> int:
+        """The next call's epoch (1, 2, 3, ...).  The device compares epochs
+        modulo 2**32 and treats the first two calls as having no earlier call
+        to wait for, so the counter never wraps: after 2**32 - 1 calls the
+        workspace restarts at 1 (``restart_epochs``, collective: every rank
+        reaches it on the same call)."""
+        if self.epoch >= EPOCH_LIMIT:
+            self.restart_epochs()
         self.epoch += 1
         return self.epoch
+
+    def restart_epochs(self) -> None:
+        """Drain this device, zero the control words (counts, flags, epochs,
+        counters) on every rank, and start the epochs again; the barriers
+        keep any rank from launching before every rank has zeroed."""
+        torch.cuda.synchronize(self.key.device)
+        if self.world > 1:
+            _barrier(self.group)
+        self._reset_control()
+        if self.world > 1:
+            _barrier(self.group)
+        self.epoch = 0
+
+    def _reset_control(self) -> None:
+        stream = torch.cuda.current_stream(self.key.device)
+        N.check(N.lib().moe_ep_workspace_reset(self.base, ctypes.byref(self.layout),
+                                               ctypes.c_void_p(stream.cuda_stream)), "moe_ep_workspace_reset")
+        torch.cuda.synchronize(self.key.device)
 
     def host_status(self) -> int:
         return int(self.status_host[0]) & 0xFFFFFFFF

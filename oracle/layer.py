@@ -38,6 +38,20 @@ def baseline_run(recv: np.ndarray, chunk: int, world_size: int, weights: np.ndar
     return np.matmul(x.astype(np.float32), weights.astype(np.float32))
 
 
+def expert_cell(tokens: np.ndarray, routing: tuple, expert: int, weights: np.ndarray,
+                rows: np.ndarray | None = None) -> np.ndarray:
+    """One (source rank, expert) cell of the layer output, in fp32: the
+    source's tokens routed to ``expert`` in ascending token order
+    (utils.py:30-32; ``routing`` = ``bucketize`` of the source's ids) times
+    the expert's weights [H, N] (baseline.py:50).  ``rows`` selects rows of
+    the cell by their index inside the bucket."""
+    counts, offsets, perm = routing
+    idx = perm[offsets[expert]:offsets[expert] + counts[expert]]
+    if rows is not None:
+        idx = idx[np.asarray(rows, np.int64)]
+    return np.asarray(tokens[idx], np.float32) @ np.asarray(weights, np.float32)
+
+
 def ep_layer(send: list[np.ndarray], chunk: int, weights: list[np.ndarray]) -> list[np.ndarray]:
     """Whole layer for all ranks: exchange, regroup, per-expert GEMM."""
     W = len(send)

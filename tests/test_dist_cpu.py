@@ -71,6 +71,28 @@ def _bound_worker(rank, world, port, q):
         q.put((rank, "error", traceback.format_exc()))
 
 
+def _epoch_worker(rank, world, port, q):
+    """A workspace whose epoch counter reaches the 32-bit limit restarts at 1
+    on every rank on the same call, zeroing its control words in between."""
+    try:
+        import types
+        import torch.distributed as dist
+        from nvshmem_testing_b200 import symm
+
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+        symm.torch.cuda.synchronize = lambda *a, **k: None  # no device here
+        ws = object.__new__(symm.SymmetricWorkspace)
+        ws.key = types.SimpleNamespace(device=0)
+        ws.world, ws.group, ws.epoch = world, None, symm.EPOCH_LIMIT - 2
+        resets = []
+        ws._reset_control = lambda: resets.append(ws.epoch)
+        seq = [ws.next_epoch() for _ in range(4)]
+        dist.destroy_process_group()
+        q.put((rank, "ok", (seq, resets)))
+    except Exception:
+        q.put((rank, "error", traceback.format_exc()))
+
+
 def _run(target, world):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
@@ -113,3 +135,12 @@ def test_general_bound_is_all_reduced():
         assert rows == (11 if r == 0 else 15)
         assert bound == 9
         assert zeros == (0, 1)  # empty counts: bound at least 1
+
+
+def test_epochs_restart_before_the_32_bit_limit():
+    res = _run(_epoch_worker, 2)
+    for r, (kind, payload) in res.items():
+        assert kind == "ok", payload
+        seq, resets = payload
+        assert seq == [2**32 - 2, 2**32 - 1, 1, 2]
+        assert resets == [2**32 - 1]

@@ -71,14 +71,28 @@ def _worker(rank, world, port, cases, q):
                 for le in range(El):
                     valid[le, src * gm:src * gm + rcm[src, le]] = True
             errs = []
-            for k, o_ in enumerate(outs):
+
+            def check(label, o_):
                 o_ = o_.float().cpu().numpy()
                 good = np.allclose(o_[valid], ref[valid], rtol=RTOL, atol=ATOL)
                 scale = max(float(np.abs(ref[valid]).max()), 1e-6)
                 rel = float(np.abs(o_[valid] - ref[valid]).max()) / scale
                 zeros = not o_[~valid].any()
                 if not (good and rel <= 1e-2 and zeros):
-                    errs.append(f"call {k}: allclose={good} rel={rel:.3e} zero_padding={zeros}")
+                    errs.append(f"{label}: allclose={good} rel={rel:.3e} zero_padding={zeros}")
+
+            for k, o_ in enumerate(outs):
+                check(f"call {k}", o_)
+            # dispatch placements: CTAs that only push, local tiles first
+            for pc, lf in ((8, El // 2), (2, El)):
+                for k in range(2):
+                    check(f"push_ctas={pc} local_first={lf} call {k}",
+                          apg.run(rank, coal, chunk, 1, wl.T, wl.H, wl.E, world, None, False, w.cuda(), rc,
+                                  timeout_s=10.0, push_ctas=pc, local_first=lf))
+            # from token rows and ids, counts exchanged inside the kernel
+            for k in range(2):
+                check(f"layer call {k}", apg.layer(tok.cuda(), ids.cuda(), wl.E, w.cuda(), timeout_s=10.0,
+                                                   push_ctas=2 * k))
             # the same layer through the unpadded (general) exchange
             coal_c, total, lengths_c = utils.dispatch(tok.cuda(), ids.cuda(), wl.E, world, general_a2a=True)
             assert lengths_c == lengths and total == sum(lengths)
