@@ -144,7 +144,9 @@ struct RowMaps {
   CUtensorMap m[kRowMaps];  // box {64, 8 << i}
 };
 
-struct Sched {
+// Sched and Smem sit back to back in shared memory; both are 16-byte
+// aligned (Smem holds the 8-byte mbarriers) whatever their arrays add up to.
+struct alignas(16) Sched {
   int nfeat, kblocks;
   int tiles_total, push_total, zero_total;
   int cnt[kMaxCells];                     // [src][le] rows this rank receives
@@ -164,7 +166,7 @@ struct Sched {
   int ooff[kMaxCells + 1];                // compact mode: [le][src] first output row of the cell
 };
 
-struct Smem {
+struct alignas(16) Smem {
   uint64_t full[kStages];   // leader: both CTAs' bytes for the stage landed
   uint64_t empty[kStages];  // each CTA: the pair MMA finished reading the stage
   uint64_t tfull[2];        // each CTA: accumulator ready
@@ -1035,6 +1037,8 @@ struct DeviceLaunchInfo {
 };
 static DeviceLaunchInfo g_launch_info[kMaxDevices];
 
+static_assert(sizeof(Sched) % 16 == 0 && kEpiStageBytes % 16 == 0 && (kStages * kStageBytes) % 1024 == 0,
+              "Sched and Smem must start on 16-byte boundaries");
 // The whole shared-memory plan must fit the 227 KB a CTA may opt in to.
 static_assert(1024 + size_t(kStages) * kStageBytes + kEpiStageBytes + sizeof(Sched) + sizeof(Smem) <= 227 * 1024,
               "shared memory plan exceeds 227 KB");
