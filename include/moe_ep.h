@@ -10,6 +10,8 @@
  * Which reference interface each entry point replaces (paths are within the
  * jy1534/nvshmem_testing project):
  *   moe_route, moe_pack_padded  utils.py:28-69  (bucketize, pad, coalesce)
+ *   moe_publish_i32             utils.py:45-49  (the largest bucket, read on
+ *                               the host to size the padded chunk)
  *   moe_symm_*                  alltoall_persistent_gemm.py:161-204
  *                               (_get_symm_buffers: symmetric receive and
  *                               signal buffers, rendezvous)
@@ -98,6 +100,15 @@ int moe_router(const void* x, int64_t T, int32_t H, const void* router_w, int32_
  *                    outside [0, E) or repeats an earlier id of the row. */
 int moe_route_slots(const void* top_idxs, int ids_are_int64, int64_t T, int K, int E, int32_t* counts,
                     int32_t* offsets, int32_t* perm, int32_t* slots, int32_t* max_count, void* stream);
+
+/* Copies n int32 words from src (device) to dst with a kernel, in stream
+ * order.  For sizes computed on the device that the host must read before
+ * it can size the next buffers (utils.py:45-49: the largest bucket decides
+ * the padded chunk): dst may be pinned host memory, which the GPU writes over
+ * PCIe without a copy engine, so the host's wait (an event after this call)
+ * does not queue behind a bulk device-to-host copy on another stream.
+ * n <= 2^20. */
+int moe_publish_i32(const int32_t* src, int64_t n, int32_t* dst, void* stream);
 
 /* Replaces utils.py:54-69: out[e*gm + j, :] = tokens[perm[offsets[e] + j], :]
  * for j < counts[e] and zero rows for counts[e] <= j < gm.  Requires

@@ -24,7 +24,7 @@ EXPORTED = ["moe_ep_abi_version", "moe_ep_status_string", "moe_ep_num_sms", "moe
             "moe_symm_alloc", "moe_symm_import", "moe_symm_free", "moe_ep_workspace_layout", "moe_ep_workspace_reset", "moe_ep_run",
             "moe_ep_read_status", "moe_ep_run_noalloc", "moe_route_slots", "moe_ep_workspace_layout_ret",
             "moe_ep_run_combine", "moe_pack_compact", "moe_ep_run_compact", "moe_router", "moe_swiglu",
-            "moe_ep_run_compact_swiglu"]
+            "moe_ep_run_compact_swiglu", "moe_publish_i32"]
 
 
 class MoeEpError(RuntimeError):
@@ -107,6 +107,7 @@ def lib() -> ctypes.CDLL:
     L.moe_router.argtypes = [c_vp, c_i64, ctypes.c_int32, c_vp, ctypes.c_int32, ctypes.c_int32, c_vp, c_vp,
                              ctypes.c_int32, c_vp, c_vp]
     L.moe_ep_read_status.argtypes = [c_u64, P(Layout), P(ctypes.c_uint32)]
+    L.moe_publish_i32.argtypes = [c_vp, c_i64, c_vp, c_vp]
     for name in EXPORTED:
         if name not in ("moe_ep_status_string",):
             getattr(L, name).restype = c_int

@@ -54,6 +54,11 @@ int moe_route_slots(const void* top_idxs, int ids_are_int64, int64_t T, int K, i
                       static_cast<cudaStream_t>(stream));
 }
 
+int moe_publish_i32(const int32_t* src, int64_t n, int32_t* dst, void* stream) {
+  if (n < 0 || (n > 0 && (!src || !dst)) || n > (int64_t(1) << 20)) return kBadArg;
+  return launch_publish_i32(src, n, dst, static_cast<cudaStream_t>(stream));
+}
+
 int moe_pack_padded(const void* tokens, int64_t H, int elem_bytes, const int32_t* counts, const int32_t* offsets,
                     const int32_t* perm, int E, int64_t gm, void* out, void* stream) {
   if (H <= 0 || elem_bytes <= 0 || (H * elem_bytes) % 16 || E < 1 || gm < 0 || !counts || !offsets || !out)

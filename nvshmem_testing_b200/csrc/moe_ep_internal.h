@@ -47,6 +47,7 @@ struct LocalWords {
   uint32_t pad;
 };
 
+int launch_publish_i32(const int32_t* src, int64_t n, int32_t* dst, cudaStream_t stream);
 int launch_pack_compact(const void* tokens, int64_t H, int elem_bytes, const int32_t* perm, int64_t rows, void* out,
                         int num_sms, cudaStream_t stream);
 int launch_pack_padded(const void* tokens, int64_t H, int elem_bytes, const int32_t* counts, const int32_t* offsets,

@@ -209,6 +209,19 @@ __global__ void pack_compact_kernel(const uint4* __restrict__ tokens, int64_t ro
   }
 }
 
+// n int32 words from src to dst by one warp (dst may be mapped pinned host
+// memory: the stores cross PCIe without a copy engine).
+__global__ void publish_i32_kernel(const int32_t* __restrict__ src, int64_t n, int32_t* dst) {
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) *reinterpret_cast<volatile int32_t*>(dst + i) = src[i];
+  __threadfence_system();
+}
+
+int launch_publish_i32(const int32_t* src, int64_t n, int32_t* dst, cudaStream_t stream) {
+  if (n == 0) return kOk;
+  publish_i32_kernel<<<1, 32, 0, stream>>>(src, n, dst);
+  return cudaGetLastError() == cudaSuccess ? kOk : kCudaErr;
+}
+
 size_t route_smem_bytes(int E) { return size_t(E) * (4 + 4 + 4 * kRouteWords + 2 * kRouteWords); }
 
 int launch_route(const void* ids, int ids_are_int64, int64_t T, int K, int E, int32_t* counts, int32_t* offsets,

@@ -94,11 +94,21 @@ def pack_compact(tokens: torch.Tensor, r: Routing, rows: int | None = None) -> t
 
 def global_max_count(r: Routing, group=None) -> int:
     """All-reduced (MAX) largest bucket; at least 1 like the reference, whose
-    empty buckets carry a one-row placeholder (utils.py:36-41)."""
+    empty buckets carry a one-row placeholder (utils.py:36-41).
+
+    The one host read of the routing: a kernel writes the value into pinned
+    host memory (``moe_publish_i32``) and the host waits for an event after
+    it, i.e. for this stream's work only — not behind a bulk device-to-host
+    copy that another stream may have queued on the copy engines."""
     m = r.max_count.clone()
     if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
         dist.all_reduce(m, op=dist.ReduceOp.MAX, group=group)
-    return max(int(m.item()), 1)
+    host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+    N.check(N.lib().moe_publish_i32(m.data_ptr(), 1, host.data_ptr(), _stream_ptr(m.device)), "moe_publish_i32")
+    done = torch.cuda.Event()
+    done.record(torch.cuda.current_stream(m.device))
+    done.synchronize()
+    return max(int(host[0]), 1)
 
 
 def dispatch(tokens: torch.Tensor, top_idxs: torch.Tensor, num_experts: int, world_size: int, group=None,
