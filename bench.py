@@ -564,33 +564,36 @@ def nvlink_probe(case: LayerCase) -> dict | None:
     kind = cr.cudaMemcpyKind.cudaMemcpyDeviceToDevice
     streams = [torch.cuda.Stream(case.dev) for _ in range(W - 1)]
     res = {}
-    for pattern in ("ring", "all_to_all"):
+    part = nbytes // (W - 1) // 4096 * 4096
+    for pattern in ("ring", "all_to_all", "shifts"):
         def go():
-            if pattern == "ring":
+            if pattern == "ring":  # every rank to its neighbour: a permutation
                 peers = [((me + 1) % W, nbytes, streams[0])]
-            else:
-                part = nbytes // (W - 1) // 4096 * 4096
+            elif pattern == "all_to_all":  # every rank to every peer at once
                 peers = [((me + q) % W, part, streams[q - 1]) for q in range(1, W)]
+            else:  # W-1 permutations one after another (shift by q), one stream
+                peers = [((me + q) % W, part, streams[0]) for q in range(1, W)]
             for d, n, st in peers:
                 # senders to one peer write disjoint parts of its receive region
-                dst = int(bases[d]) + int(ws.layout.off_data) + (me * n if pattern == "all_to_all" else 0)
+                dst = int(bases[d]) + int(ws.layout.off_data) + (me * n if pattern != "ring" else 0)
                 err, = cr.cudaMemcpyAsync(dst, src, n, kind, st.cuda_stream)
                 if err != cr.cudaError_t.cudaSuccess:
                     raise RuntimeError(f"cudaMemcpyAsync: {err}")
             cur = torch.cuda.current_stream(case.dev)
-            for _, _, st in peers:
+            for st in {id(x[2]): x[2] for x in peers}.values():
                 cur.wait_stream(st)
         try:
             for _ in range(2):
                 go()
             ms, _ = time_device(go, 5, 1)
             ms = max_over_ranks(ms)
-            moved = nbytes if pattern == "ring" else (nbytes // (W - 1) // 4096 * 4096) * (W - 1)
+            moved = nbytes if pattern == "ring" else part * (W - 1)
             res[f"{pattern}_gbs"] = moved / (ms * 1e-3) / 1e9
         except Exception as exc:
             res[f"{pattern}_error"] = str(exc)[:200]
     res["bytes"] = nbytes
-    res["what"] = "copy-engine cudaMemcpyAsync into peers' cuMem-mapped workspaces, all ranks at once"
+    res["what"] = ("copy-engine cudaMemcpyAsync into peers' cuMem-mapped workspaces, all ranks at once: ring (one "
+                   "peer), all_to_all (W-1 peers at once), shifts (W-1 permutations in turn)")
     return res
 def run_mlp_path(args) -> int:
     """The full expert MLP (``mlp.run``: compact exchange + [gate|up] GEMM,
@@ -1121,6 +1124,7 @@ def main(argv=None) -> int:
                    "local_experts": case.El, "top_k": wl.K, "out_dim": wl.N, "routing": wl.routing, "gm": case.gm,
                    "parallelism": f"ep{world}", "l2": "inputs larger than L2 (weights and tokens > 126 MB)",
                    "push_ctas": apg.placement(world, case.El)[0], "local_first": apg.placement(world, case.El)[1],
+                   "push_warps": apg.push_setup()[0], "push_mode": apg.push_setup()[1],
                    "push_rows": apg.DEFAULT_PUSH_ROWS},
         "parity_vs_nccl_allclose": head["parity_vs_nccl_allclose"],
         "parity_oracle": parity,
@@ -1152,6 +1156,10 @@ def main(argv=None) -> int:
             rf = r["roofline"]
             r["roofline"] = {k: rf[k] for k in ("bound", "frac", "layer_roofline_us", "layer_frac", "bounds_us")}
             r["parity_oracle"] = None if args.no_oracle else c2.oracle_check([c2.El // 2], 16, send_buffer=False)
+            tl2 = c2.timeline()
+            slow = max(tl2, key=lambda t: t["layer_us"])
+            r["timeline_slowest_rank"] = {k: slow.get(k) for k in ("layer_us", "counts_us", "sched_us", "push_end_us",
+                                                                   "nvlink_out_gbs", "gemm_end_us", "flag_wait_us")}
             others.append(r)
             del c2
             torch.cuda.synchronize()

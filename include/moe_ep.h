@@ -84,14 +84,20 @@ int moe_route(const void* top_idxs, int ids_are_int64, int64_t T, int K, int E, 
  *   top_idxs [T, K]    = the K most probable experts, descending, equal
  *                        probabilities by ascending id (int64 or int32)
  *   top_vals [T, K]    = their probabilities (bf16 values as float32)
- * `logits` is caller-provided scratch (16-byte aligned).  Requires H % 8 == 0,
- * 8 <= E <= 1024 with E % 8 == 0, 1 <= K <= min(E, 32).  The GEMM's control
- * words live in a fixed 2 KB array inside the library, so the call allocates
- * nothing; every call reuses that array, so router calls must not overlap
- * each other on the GPU, and the first call on a device looks the array up
- * synchronously (make it before any stream capture). */
+ * `logits` receives the bf16 logits (16-byte aligned).  Requires H % 8 == 0,
+ * 8 <= E <= 1024 with E % 8 == 0, 1 <= K <= min(E, 32).  Allocates nothing.
+ * E <= 256: one kernel (split-K clusters on the tensor cores, the partial
+ * logits reduced through distributed shared memory, softmax and top-k in its
+ * epilogue); it keeps no state between calls, so calls may overlap.
+ * E > 256: the fused layer kernel's GEMM, whose control words live in a
+ * fixed 2 KB array inside the library, then a softmax/top-k kernel; such
+ * calls must not overlap each other on the GPU, and the first one on a
+ * device looks the array up (make it before any stream capture).
+ * status_host: optional mapped pinned word that receives a device-side error
+ * (a pipeline wait that exceeded its bound), encoded as the workspace status
+ * word; NULL discards it. */
 int moe_router(const void* x, int64_t T, int32_t H, const void* router_w, int32_t E, int32_t K, void* logits,
-               void* top_idxs, int32_t ids_are_int64, float* top_vals, void* stream);
+               void* top_idxs, int32_t ids_are_int64, float* top_vals, int32_t* status_host, void* stream);
 
 /* moe_route plus, for the return path,
  *   slots     [T, K] int32: j such that perm[offsets[e] + j] = t for
@@ -198,8 +204,19 @@ typedef struct moe_ep_run_params {
                                /* instead of its receive counts; the kernel's own   */
                                /* count exchange then replaces the host-side count  */
                                /* all-to-all of benchmark.py:114-118                */
+  int32_t push_warps;          /* push_ctas == 0: warps of every CTA that move rows */
+                               /* (1..6; 0 = 2)                                     */
+  int32_t push_mode;           /* MOE_EP_PUSH_* bits                                */
   int32_t reserved0;           /* 0                                                 */
 } moe_ep_run_params;
+
+/* push_mode bits.  BULK: push CTAs move rows with TMA bulk copies (local rows
+ * through a ring of shared-memory pieces to the peer) instead of loads and
+ * stores.  BY_DESTINATION: senders go through destinations one at a time
+ * (me-1, me-2, ...; experts in order within each) instead of finishing each
+ * expert for every destination before the next. */
+#define MOE_EP_PUSH_BULK 1
+#define MOE_EP_PUSH_BY_DESTINATION 2
 
 /* Device timeline (globaltimer ns, or counts), one record per CTA. */
 #define MOE_EP_TRACE_WORDS 24

@@ -17,6 +17,7 @@ STATUS_NAMES = {OK: "ok", BAD_ARG: "bad argument", CUDA_ERR: "CUDA error", TIMEO
                 CAPACITY: "receive capacity exceeded", BAD_ROUTE: "bad routing input",
                 SCRATCH_LIMIT: "size exceeds the fixed scratch of moe_ep_run_noalloc"}
 NOALLOC_MAX_EXPERTS = 64
+PUSH_BULK, PUSH_BY_DESTINATION = 1, 2
 ABI_VERSION = 3
 
 # Every symbol include/moe_ep.h declares.
@@ -52,7 +53,8 @@ class RunParams(ctypes.Structure):
                 ("max_chunks", ctypes.c_int32), ("epoch", ctypes.c_uint32), ("num_ctas", ctypes.c_uint32),
                 ("timeout_ns", ctypes.c_uint64), ("status_host", ctypes.c_void_p), ("trace", ctypes.c_void_p),
                 ("push_ctas", ctypes.c_int32), ("local_first", ctypes.c_int32),
-                ("counts_are_send", ctypes.c_int32), ("reserved0", ctypes.c_int32)]
+                ("counts_are_send", ctypes.c_int32), ("push_warps", ctypes.c_int32), ("push_mode", ctypes.c_int32),
+                ("reserved0", ctypes.c_int32)]
 
 
 class CombineParams(ctypes.Structure):
@@ -105,7 +107,7 @@ def lib() -> ctypes.CDLL:
     L.moe_swiglu.argtypes = [c_vp, c_i64, ctypes.c_int32, c_vp, c_vp]
     L.moe_ep_run_compact_swiglu.argtypes = [P(RunParams), c_i64, c_i64, c_vp]
     L.moe_router.argtypes = [c_vp, c_i64, ctypes.c_int32, c_vp, ctypes.c_int32, ctypes.c_int32, c_vp, c_vp,
-                             ctypes.c_int32, c_vp, c_vp]
+                             ctypes.c_int32, c_vp, c_vp, c_vp]
     L.moe_ep_read_status.argtypes = [c_u64, P(Layout), P(ctypes.c_uint32)]
     L.moe_publish_i32.argtypes = [c_vp, c_i64, c_vp, c_vp]
     for name in EXPORTED:

@@ -44,6 +44,8 @@ DEFAULT_TIMEOUT_S = float(os.environ.get("MOE_EP_TIMEOUT_S", "20"))
 # two push warps in every CTA), and experts whose local tiles run first.
 DEFAULT_PUSH_CTAS = int(os.environ.get("MOE_EP_PUSH_CTAS", "0"))
 DEFAULT_LOCAL_FIRST = int(os.environ.get("MOE_EP_LOCAL_FIRST", "0"))
+DEFAULT_PUSH_WARPS = int(os.environ.get("MOE_EP_PUSH_WARPS", "2"))
+DEFAULT_PUSH_MODE = int(os.environ.get("MOE_EP_PUSH_MODE", "0"))
 
 
 def placement(W: int, El: int, push_ctas: int | None = None, local_first: int | None = None) -> tuple[int, int]:
@@ -57,6 +59,17 @@ def placement(W: int, El: int, push_ctas: int | None = None, local_first: int | 
     if pc < 0 or pc % 2:
         raise ValueError(f"push_ctas must be even and >= 0, got {pc}")
     return pc, max(0, min(lf, El))
+
+
+def push_setup(push_warps: int | None = None, push_mode: int | None = None) -> tuple[int, int]:
+    """(push_warps, push_mode): warps per CTA that move rows when no push
+    CTAs are used, and the MOE_EP_PUSH_* bits (bulk copies in push CTAs,
+    destination-major order)."""
+    pw = DEFAULT_PUSH_WARPS if push_warps is None else int(push_warps)
+    pm = DEFAULT_PUSH_MODE if push_mode is None else int(push_mode)
+    if not 1 <= pw <= 6 or pm & ~3:
+        raise ValueError(f"push_warps must be 1..6 and push_mode a combination of bits 1 and 2, got {pw}, {pm}")
+    return pw, pm
 
 
 def _group_info(group, world_size: int, rank: int) -> tuple[int, int]:
@@ -76,7 +89,8 @@ def raise_if_device_error(ws) -> None:
 def _launch_params(me: int, W: int, tokens: torch.Tensor, gm: int | None, transmit_size: int, hidden_dim: int,
                    local_weights: torch.Tensor, recv_counts, group, timeout_s, push_rows, num_ctas, trace,
                    ret_cols: int = 0, push_ctas: int | None = None, local_first: int | None = None,
-                   send_counts: torch.Tensor | None = None):
+                   send_counts: torch.Tensor | None = None, push_warps: int | None = None,
+                   push_mode: int | None = None):
     """Validate the fused layer's inputs and fill ``moe_ep_run_params``.
 
     ``gm`` is the bound on every (rank, expert) count; ``None`` means the
@@ -126,6 +140,7 @@ def _launch_params(me: int, W: int, tokens: torch.Tensor, gm: int | None, transm
     p.epoch = ws.next_epoch()
     p.num_ctas = num_ctas
     p.push_ctas, p.local_first = placement(W, El, push_ctas, local_first)
+    p.push_warps, p.push_mode = push_setup(push_warps, push_mode)
     p.counts_are_send = int(send_counts is not None)
     p.timeout_ns = int((timeout_s if timeout_s is not None else DEFAULT_TIMEOUT_S) * 1e9)
     p.status_host = ws.status_host.data_ptr()
@@ -155,7 +170,8 @@ def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: in
         timeout_s: float | None = None, push_rows: int | None = None, num_ctas: int = 0,
         check: bool = False, trace: torch.Tensor | None = None, max_count: int | None = None,
         recv_rows: int | None = None, push_ctas: int | None = None, local_first: int | None = None,
-        send_counts: torch.Tensor | None = None) -> torch.Tensor:
+        send_counts: torch.Tensor | None = None, push_warps: int | None = None,
+        push_mode: int | None = None) -> torch.Tensor:
     """Fused dispatch + grouped GEMM; see the module docstring.
 
     ``general_a2a=True`` (a stub in the reference, alltoall_persistent_gemm.py:221-222)
@@ -177,6 +193,7 @@ def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: in
     ``trace`` (int64 device tensor of at least ``num_sms * 24`` words that
     receives the per-CTA device timeline, ``_native.TRACE_FIELDS``),
     ``push_ctas`` / ``local_first`` (dispatch placement, see ``placement``),
+    ``push_warps`` / ``push_mode`` (how rows move, see ``push_setup``),
     ``send_counts`` (padded path only: this rank's ``[W*El]`` per-expert
     counts, i.e. the routing's ``lengths``, in place of ``recv_counts``; the
     kernel's count exchange then replaces the count all-to-all of
@@ -203,7 +220,8 @@ def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: in
             tokens = torch.zeros((1, tokens.shape[1]), dtype=tokens.dtype, device=tokens.device)
         ws, p, (El, gm, Nout), keep = _launch_params(me, W, tokens, gm, transmit_size, hidden_dim, local_weights,
                                                      recv_counts, group, timeout_s, push_rows, num_ctas, trace,
-                                                     push_ctas=push_ctas, local_first=local_first)
+                                                     push_ctas=push_ctas, local_first=local_first,
+                                                     push_warps=push_warps, push_mode=push_mode)
         # A zero-row view has a null data_ptr; the kernel wants a real buffer.
         buf = torch.empty((max(out_rows, 1), Nout), dtype=torch.bfloat16, device=tokens.device)
         out = buf[:out_rows]
@@ -216,7 +234,8 @@ def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: in
         ws, p, (El, gm, Nout), keep = _launch_params(me, W, tokens, None, transmit_size, hidden_dim, local_weights,
                                                      recv_counts, group, timeout_s, push_rows, num_ctas, trace,
                                                      push_ctas=push_ctas, local_first=local_first,
-                                                     send_counts=send_counts)
+                                                     send_counts=send_counts, push_warps=push_warps,
+                                                     push_mode=push_mode)
         out = torch.empty((El, W * gm, Nout), dtype=torch.bfloat16, device=tokens.device)
         p.out = out.data_ptr()
         stream = torch.cuda.current_stream(tokens.device)

@@ -66,10 +66,17 @@ constexpr int kFeatPair = 256;                  // output features per pair tile
 constexpr int kFeatCta = 128;                   // features per CTA (TMEM lanes)
 constexpr int kMaxTileRows = 256;               // rows per tile (MMA N)
 constexpr int kEpiWarps = 4;
-constexpr int kPushWarps = 2;                   // enough to stay ahead of the GEMM; more slow it down (L2 contention)
+constexpr int kMaxPushWarps = 6;                // push warps present in every CTA (Params::push_warps of them work)
 constexpr int kWarpProducer = 0, kWarpMma = 1, kWarpEpi0 = 2, kWarpPush0 = 2 + kEpiWarps;
-constexpr int kThreads = (2 + kEpiWarps + kPushWarps) * 32;
-constexpr int kPushThreads = kPushWarps * 32;
+constexpr int kThreads = (2 + kEpiWarps + kMaxPushWarps) * 32;
+constexpr int kZeroWarps = 2;                   // computing CTAs' warps that zero padded rows when push CTAs exist
+// Push CTAs in bulk mode: kBulkStreams warps, each with a ring of
+// kBulkSlots pieces of kBulkPiece bytes in the CTA's stage memory; loads run
+// kBulkLead pieces ahead of the stores.
+constexpr int kBulkStreams = 3;
+constexpr int kBulkSlots = 8;
+constexpr uint32_t kBulkPiece = 8192;
+constexpr int kBulkLead = 6;
 constexpr uint32_t kABox = 64 * KB * 2;                       // 16 KB: 64 features x 128 K
 constexpr uint32_t kABytes = kFeatCta * KB * 2;               // 32 KB
 constexpr uint32_t kBHalf = (kMaxTileRows / 2) * BK * 2;      // 16 KB: 128 rows x 64 K
@@ -121,6 +128,12 @@ struct Params {
   // only move rows to peers and zero padded rows, with all their warps; the
   // others only compute.  0: two push warps in every CTA.
   int push_ctas;
+  int push_warps;  // push warps per computing CTA when push_ctas == 0 (1..kMaxPushWarps)
+  int push_bulk;   // push CTAs copy through the TMA engine (bulk copies) instead of loads and stores
+  // Push order: 0 = expert-major (every sender finishes expert le for all
+  // destinations before le+1); 1 = destination-major (q = 1..W-1, destination
+  // me - q, experts in order within each).
+  int push_phased;
   // Tile order: the local tiles of experts [0, local_first) come before any
   // remote tile, so the GEMM starts on rows that need no NVLink transfer.
   int local_first;
@@ -173,10 +186,13 @@ struct alignas(16) Smem {
   uint64_t tempty[2];       // leader: both CTAs' epilogues drained the accumulator
   uint64_t go[kGoSlots];    // peer: the leader's verdict for a tile
   uint64_t drain;
+  uint64_t bulk[kBulkStreams][kBulkSlots];  // push CTAs, bulk mode: a ring slot's load landed
   int go_tile[kGoSlots];    // the tile the leader handed out for this slot, or -1 (stop)
   uint32_t tmem_base;
   int abort_flag;
   int push_item;
+  int zero_item;
+  unsigned long long push_items, push_bytes, push_end;  // this CTA's dispatch (timeline)
   uint32_t fills[kStages];
   uint32_t cons[kStages];
 };
@@ -250,6 +266,22 @@ __device__ __forceinline__ int find_cell(const int* pfx, int ncells, int t) {
     else hi = mid - 1;
   }
   return lo;
+}
+
+// Push items are counted per cell (expert le, position q = 1..W-1 where the
+// destination is me - q), then per chunk; the cell order is expert-major or
+// destination-major (Params::push_phased).
+__device__ __forceinline__ int push_cell(const Params& p, int le, int qi) {
+  return p.push_phased ? qi * p.El + le : le * (p.W - 1) + qi;
+}
+__device__ __forceinline__ void push_cell_decode(const Params& p, int c, int& le, int& q) {
+  if (p.push_phased) {
+    le = c % p.El;
+    q = c / p.El + 1;
+  } else {
+    le = c / (p.W - 1);
+    q = c % (p.W - 1) + 1;
+  }
 }
 
 __device__ int wait_tile(Smem& sm, uint32_t ti, uint64_t bound_ns) {
@@ -377,7 +409,7 @@ __device__ void build_schedule(const Params& p, Sched& s, Smem& sm) {
       s.soff[i] = C(d, me, le);          // scanned below (cells d-major)
       s.ooff[le * W + d] = s.cnt[i];     // scanned below (cells le-major)
     }
-    if (d != me) s.push_pfx[le * (W - 1) + (q_me - 1)] = (sc + p.push_rows - 1) / p.push_rows;
+    if (d != me) s.push_pfx[push_cell(p, le, q_me - 1)] = (sc + p.push_rows - 1) / p.push_rows;
   }
   __syncthreads();
 
@@ -406,10 +438,10 @@ __device__ void build_schedule(const Params& p, Sched& s, Smem& sm) {
   // Prefix sums, one warp each:
   //  * rbase: compact base of each expert in this rank's receive buffer;
   //  * tile_pfx: tiles, expert-major (see decode_tile);
-  //  * push_pfx: push items, expert-major — experts, then positions
-  //    q = 1..W-1 (destination d = me - q), then row chunks.  Every sender
-  //    finishes an expert's rows for all destinations before the next
-  //    expert, matching the expert-major order of the receivers' tiles;
+  //  * push_pfx: push items per cell (push_cell), then row chunks.  In the
+  //    expert-major order every sender finishes an expert's rows for all
+  //    destinations before the next expert, matching the expert-major order
+  //    of the receivers' tiles;
   //  * push_off (per destination d, warps 3..): where my rows for (d, le)
   //    land at d = d's compact base of le + the rows that precede mine.
   if (warp == 0) {
@@ -477,6 +509,18 @@ __device__ __forceinline__ unsigned char* ret_row_ptr(const Sched& s, const Para
          ((int64_t(p.me) * p.El + tl.le) * p.gm + i) * int64_t(p.N) * 2;
 }
 
+// Zero one padded output cell's rows past its count (padded mode): z =
+// le * W + src; np threads, pt = this thread.
+__device__ void zero_fill(const Params& p, const Sched& s, int z, int pt, int np) {
+  const int W = p.W, El = p.El;
+  const int le = z / W, src = z % W;
+  const int64_t c0 = s.cnt[src * El + le];
+  const int64_t nvec = (p.gm - c0) * int64_t(p.N) / 8;
+  uint4* dst = reinterpret_cast<uint4*>(p.out + (int64_t(le) * W * p.gm + int64_t(src) * p.gm + c0) * p.N);
+  const uint4 zv = make_uint4(0, 0, 0, 0);
+  for (int64_t v = pt; v < nvec; v += np) dst[v] = zv;
+}
+
 // One push item's rows: nvec 16-byte vectors from this GPU's send buffer to
 // a peer's receive region, U loads in flight per thread before their stores.
 template <int U>
@@ -530,7 +574,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       sm.go_tile[i] = -1;
     }
     mbar_init(&sm.drain, 1);
+    for (int i = 0; i < kBulkStreams; ++i)
+      for (int j = 0; j < kBulkSlots; ++j) mbar_init(&sm.bulk[i][j], 1);
     sm.abort_flag = 0;
+    sm.push_items = sm.push_bytes = sm.push_end = 0ull;
     fence_mbar_init();
     prefetch_tensormap(&tm_w);
   }
@@ -549,8 +596,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   // every rank; every CTA then waits for all W blocks.  One rank has nothing
   // to exchange: the schedule reads recv_counts directly, and each CTA only
   // waits until the call that last used this epoch parity has finished.
-  if (W > 1 && blockIdx.x == 0 && warp == kWarpPush0) {
-    for (int d = 0; d < W; ++d) {
+  // Warp w of CTA 0 publishes to ranks w, w + 12, ...: the W system-scope
+  // fences run side by side.
+  if (W > 1 && blockIdx.x == 0) {
+    for (int d = warp; d < W; d += kThreads / 32) {
       unsigned char* peer = reinterpret_cast<unsigned char*>(p.peers[d]);
       int go = 1;
       if (lane == 0) {
@@ -586,9 +635,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool run_main = !aborted(sm);
   if (tid == 0) TRACE_SET(p, MOE_EP_TRACE_SCHED, TRACE_NOW(p));
 
-  // Rows are pushed by two warps of every CTA, or by every warp of the push
-  // CTAs; the other warps of push CTAs have no role.
-  const bool pusher = push_cta || (p.push_ctas == 0 && warp >= kWarpPush0);
+  // Rows are pushed by push_warps warps of every CTA, or by the push CTAs
+  // (every warp, or kBulkStreams bulk-copy streams).
+  const bool pusher = push_cta || (p.push_ctas == 0 && warp >= kWarpPush0 && warp < kWarpPush0 + p.push_warps);
   if (run_main && !push_cta && warp == kWarpProducer) {
     if (lane == 0) {
       const uint32_t bar_leader0 = mapa_shared(smem_u32(&sm.full[0]), 0);
@@ -813,18 +862,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       TRACE_SET(p, MOE_EP_TRACE_EPI_END, TRACE_NOW(p));
       TRACE_SET(p, MOE_EP_TRACE_EPI_WAIT, epi_ns);
     }
-  } else if (run_main && pusher) {
-    const int np = push_cta ? kThreads : kPushThreads;  // threads taking part in each item
+  } else if (run_main && pusher && !(push_cta && p.push_bulk)) {
+    // Loads and stores: push_warps warps of every computing CTA, or every
+    // warp of a push CTA.  Without push CTAs the same warps then zero the
+    // padded output rows (items after the push items).
+    const int np = push_cta ? kThreads : p.push_warps * 32;  // threads taking part in each item
     const int pt = push_cta ? tid : tid - kWarpPush0 * 32;
+    const int last = push_cta ? s.push_total : s.push_total + s.zero_total;
     const size_t row_bytes = size_t(p.H) * 2;
-    uint64_t items = 0, bytes = 0;
     bool pushes_done = false;
     for (;;) {
       if (pt == 0) {
         int it = aborted(sm) ? 0x7fffffff : int(atomicAdd(&lw->push_ctr[par], 1u));
         if (it < s.push_total && p.epoch > 2) {
-          const int c = find_cell(s.push_pfx, (W - 1) * El, it);
-          const int d = (me - (c % (W - 1) + 1) + W) % W;
+          int le, q;
+          push_cell_decode(p, find_cell(s.push_pfx, (W - 1) * El, it), le, q);
+          const int d = (me - q + W) % W;
           if (!wait_epoch(at_u32(p.local, p.off_free) + d, p.epoch - 2, p.timeout_ns, sm)) {
             raise_error(p, sm, kTimeout, kSiteFree, d);
             it = 0x7fffffff;
@@ -837,7 +890,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       named_bar_sync(kNamedBarPush, np);
       if (item < s.push_total) {
         const int c = find_cell(s.push_pfx, (W - 1) * El, item);
-        const int q = c % (W - 1) + 1, le = c / (W - 1);
+        int le, q;
+        push_cell_decode(p, c, le, q);
         const int d = (me - q + W) % W;
         const int chunk = item - s.push_pfx[c];
         const int j0 = chunk * p.push_rows;
@@ -848,8 +902,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint4* dst = reinterpret_cast<uint4*>(peer + p.off_data +
                                               (size_t(par) * p.cap_rows + s.push_off[d * El + le] + j0) * row_bytes);
         const int64_t nvec = int64_t(j1 - j0) * int64_t(row_bytes / 16);
-        // More loads in flight per thread where a whole CTA pushes: the copy
-        // is bound by bytes in flight over the local load latency.
+        // More loads in flight per thread where a whole CTA pushes.
         if (push_cta) copy_rows<16>(src, dst, nvec, pt, np);
         else copy_rows<4>(src, dst, nvec, pt, np);
         fence_acq_rel_sys();
@@ -857,35 +910,122 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (pt == 0) {
           uint32_t* fl = at_u32(peer, p.off_dflag) + ((size_t(par) * W + me) * El + le) * p.max_chunks + chunk;
           st_release_sys(fl, p.epoch);
-          items += 1;
-          bytes += uint64_t(nvec) * 16;
+          atomicAdd(&sm.push_items, 1ull);
+          atomicAdd(&sm.push_bytes, static_cast<unsigned long long>(nvec) * 16ull);
         }
-      } else if (item < s.push_total + s.zero_total) {
+      } else if (item < last) {
         if (pt == 0 && !pushes_done) {
           pushes_done = true;
-          TRACE_SET(p, MOE_EP_TRACE_PUSH_END, TRACE_NOW(p));
+          atomicMax(&sm.push_end, static_cast<unsigned long long>(TRACE_NOW(p)));
         }
-        const int z = item - s.push_total;
-        const int le = z / W, src = z % W;
-        const int64_t c0 = s.cnt[src * El + le];
-        const int64_t nvec = (p.gm - c0) * int64_t(p.N) / 8;
-        uint4* dst = reinterpret_cast<uint4*>(p.out + (int64_t(le) * W * p.gm + int64_t(src) * p.gm + c0) * p.N);
-        const uint4 zv = make_uint4(0, 0, 0, 0);
-        for (int64_t v = pt; v < nvec; v += np) dst[v] = zv;
+        zero_fill(p, s, item - s.push_total, pt, np);
       } else {
         break;
       }
     }
-    if (pt == 0) {
-      if (!pushes_done) TRACE_SET(p, MOE_EP_TRACE_PUSH_END, TRACE_NOW(p));
-      TRACE_SET(p, MOE_EP_TRACE_ZERO_END, TRACE_NOW(p));
-      TRACE_SET(p, MOE_EP_TRACE_PUSH_ITEMS, items);
-      TRACE_SET(p, MOE_EP_TRACE_PUSH_BYTES, bytes);
+    if (pt == 0 && !pushes_done) atomicMax(&sm.push_end, static_cast<unsigned long long>(TRACE_NOW(p)));
+  } else if (run_main && push_cta && p.push_bulk && warp < kBulkStreams) {
+    // Bulk copies: lane 0 of each stream warp moves its items through the
+    // TMA engine — local rows into a ring of shared-memory pieces, each
+    // piece out to the peer's receive region — loads kBulkLead pieces ahead
+    // of the stores.  An item's flag is released once every store of the
+    // item has completed.
+    unsigned char* ring = stage_mem + size_t(warp) * kBulkSlots * kBulkPiece;
+    const size_t row_bytes = size_t(p.H) * 2;
+    uint32_t gp = 0;  // pieces this stream has loaded (ring slot and phase)
+    bool ok = true;
+    if (lane == 0) {
+      for (;;) {
+        int it = (!ok || aborted(sm)) ? 0x7fffffff : int(atomicAdd(&lw->push_ctr[par], 1u));
+        if (it >= s.push_total) break;
+        const int c = find_cell(s.push_pfx, (W - 1) * El, it);
+        int le, q;
+        push_cell_decode(p, c, le, q);
+        const int d = (me - q + W) % W;
+        if (p.epoch > 2 && !wait_epoch(at_u32(p.local, p.off_free) + d, p.epoch - 2, p.timeout_ns, sm)) {
+          raise_error(p, sm, kTimeout, kSiteFree, d);
+          break;
+        }
+        const int chunk = it - s.push_pfx[c];
+        const int j0 = chunk * p.push_rows;
+        const int j1 = min(j0 + p.push_rows, s.push_cnt[d * El + le]);
+        unsigned char* peer = reinterpret_cast<unsigned char*>(p.peers[d]);
+        const int64_t cell = p.general ? int64_t(s.soff[d * El + le]) : (int64_t(d) * El + le) * p.gm;
+        const unsigned char* src = reinterpret_cast<const unsigned char*>(p.tokens + (cell + j0) * p.H);
+        unsigned char* dst = peer + p.off_data + (size_t(par) * p.cap_rows + s.push_off[d * El + le] + j0) * row_bytes;
+        const uint32_t nbytes = uint32_t(j1 - j0) * uint32_t(row_bytes);
+        const int npieces = int((nbytes + kBulkPiece - 1) / kBulkPiece);
+        auto piece_len = [&](int k) { return min(kBulkPiece, nbytes - uint32_t(k) * kBulkPiece); };
+        int stored = 0;
+        for (int k = 0; k < npieces + kBulkLead && ok; ++k) {
+          const int jst = k - kBulkLead;  // piece to store: its load was issued kBulkLead iterations ago
+          if (jst >= 0 && jst < npieces) {
+            const uint32_t g = gp + uint32_t(jst);
+            if (!mbar_wait(&sm.bulk[warp][g % kBulkSlots], (g / kBulkSlots) & 1, pipe_bound, sm)) {
+              if (!aborted(sm)) raise_error(p, sm, kTimeout, kSitePipe, 20);
+              ok = false;
+              break;
+            }
+            bulk_s2g(dst + size_t(jst) * kBulkPiece, ring + (g % kBulkSlots) * kBulkPiece, piece_len(jst));
+            bulk_commit();
+            stored = jst + 1;
+          }
+          if (k < npieces) {
+            // The slot's previous store (kBulkSlots pieces back) has been
+            // read out: at most kBulkSlots - kBulkLead newer stores pending.
+            bulk_wait_read<kBulkSlots - kBulkLead>();
+            const uint32_t g = gp + uint32_t(k);
+            uint64_t* bar = &sm.bulk[warp][g % kBulkSlots];
+            mbar_arrive_expect_tx(bar, piece_len(k));
+            bulk_g2s(ring + (g % kBulkSlots) * kBulkPiece, src + size_t(k) * kBulkPiece, piece_len(k), bar);
+          }
+        }
+        if (!ok) {
+          // Wait (bounded) for the loads issued but not stored, then stop.
+          const uint64_t until = globaltimer_ns() + 1000000000ull;
+          for (int k = stored; k < npieces && k < stored + kBulkLead; ++k) {
+            const uint32_t g = gp + uint32_t(k);
+            while (!mbar_try_wait(&sm.bulk[warp][g % kBulkSlots], (g / kBulkSlots) & 1) && globaltimer_ns() < until) {
+            }
+          }
+          bulk_wait<0>();
+          break;
+        }
+        gp += uint32_t(npieces);
+        bulk_wait<0>();  // every store of the item is complete
+        fence_proxy_async_global();
+        fence_acq_rel_sys();
+        uint32_t* fl = at_u32(peer, p.off_dflag) + ((size_t(par) * W + me) * El + le) * p.max_chunks + chunk;
+        st_release_sys(fl, p.epoch);
+        atomicAdd(&sm.push_items, 1ull);
+        atomicAdd(&sm.push_bytes, static_cast<unsigned long long>(nbytes));
+      }
+      atomicMax(&sm.push_end, static_cast<unsigned long long>(TRACE_NOW(p)));
+    }
+    __syncwarp();
+  } else if (run_main && p.push_ctas > 0 && !push_cta && warp >= kWarpPush0 && warp < kWarpPush0 + kZeroWarps) {
+    // With push CTAs, the computing CTAs' first push warps zero the padded
+    // output rows (their own counter).
+    const int np = kZeroWarps * 32;
+    const int pt = tid - kWarpPush0 * 32;
+    for (;;) {
+      if (pt == 0) sm.zero_item = aborted(sm) ? 0x7fffffff : int(atomicAdd(&lw->zero_ctr[par], 1u));
+      named_bar_sync(kNamedBarPush, np);
+      const int z = sm.zero_item;
+      named_bar_sync(kNamedBarPush, np);
+      if (z >= s.zero_total) break;
+      zero_fill(p, s, z, pt, np);
     }
   }
 
   // ---- teardown: drain in-flight copies and MMAs, free TMEM, publish "free".
   __syncthreads();
+  if (tid == 0) {
+    TRACE_SET(p, MOE_EP_TRACE_PUSH_END, sm.push_end);
+    TRACE_SET(p, MOE_EP_TRACE_ZERO_END, TRACE_NOW(p));
+    TRACE_SET(p, MOE_EP_TRACE_PUSH_ITEMS, sm.push_items);
+    TRACE_SET(p, MOE_EP_TRACE_PUSH_BYTES, sm.push_bytes);
+  }
   if (aborted(sm) && !leader && tid == 0) {
     // Pair loads issued by this CTA complete on the leader's barrier; after an
     // abort give them time to land before the pair tears down (bug guard).
@@ -934,6 +1074,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (p.ret) __threadfence_system();
       else __threadfence();
       lw->push_ctr[par ^ 1] = 0;
+      lw->zero_ctr[par ^ 1] = 0;
       lw->tile_ctr[par ^ 1] = 0;
       lw->done_ctr[par ^ 1] = 0;
       __threadfence();
@@ -1071,6 +1212,7 @@ int launch_fused(const moe_ep_run_params* a, const FusedMode& m, cudaStream_t st
     return kBadArg;
   if (a->num_ctas & 1u) return kBadArg;  // CTA pairs
   if (a->push_ctas < 0 || (a->push_ctas & 1) || a->local_first < 0 || a->local_first > El) return kBadArg;
+  if (a->push_warps < 0 || a->push_warps > kMaxPushWarps || (a->push_mode & ~3)) return kBadArg;
   // Rows of the token buffer (the local TMA map's extent).
   const int64_t rows_in = m.general ? m.send_rows : int64_t(W) * El * a->gm;
   if (rows_in + kMaxTileRows > (int64_t(1) << 31) || 2 * a->cap_rows + kMaxTileRows > (int64_t(1) << 31) ||
@@ -1138,6 +1280,9 @@ int launch_fused(const moe_ep_run_params* a, const FusedMode& m, cudaStream_t st
   p.status_host = a->status_host;
   p.trace = a->trace;
   p.push_ctas = a->push_ctas;
+  p.push_warps = a->push_warps > 0 ? a->push_warps : 2;
+  p.push_bulk = (a->push_mode & MOE_EP_PUSH_BULK) != 0;
+  p.push_phased = (a->push_mode & MOE_EP_PUSH_BY_DESTINATION) != 0;
   p.local_first = a->local_first;
   p.send_counts = a->counts_are_send != 0;
 

@@ -2,18 +2,27 @@
 // logits = einsum('bh,he->be', tokens, router) in bf16, softmax over the
 // experts, top-k).
 //
-// The logits GEMM runs on the fused kernel's tcgen05 GEMM as a one-rank,
-// one-expert layer (tokens = x [T, H], weights = router [H, E], out = logits
-// [T, E] bf16: fp32 accumulation rounded once, like the reference's bf16
-// einsum).  Its control words (a one-entry peer table, the count matrix,
-// flags, counters and the status word) and its one count word live in a
-// fixed array of this file, so the router needs no workspace and allocates
-// nothing; the first call on a device looks the array's address up with
-// cudaGetSymbolAddress.  A second kernel then takes one token per warp: the
-// fp32 softmax of the bf16 logits, rounded to bf16 (the reference's softmax
-// output dtype), and the K largest probabilities in descending order, equal
-// probabilities by ascending expert id (torch.topk leaves their order
-// unspecified).
+// E <= 256: one kernel, router_kernel.  Each cluster of S CTAs (S = 1, 2, 4
+// or 8, chosen so that the grid fills the SMs) computes one 128-token tile:
+// CTA r of the cluster multiplies the tile by the r-th 1/S of the hidden
+// dimension on the tensor cores (tcgen05.mma kind::f16, M = 128 tokens,
+// N = E, fp32 accumulators in TMEM, TMA-fed 4-stage pipeline).  The S
+// partial tiles are then reduced through distributed shared memory: CTA r
+// owns rows [r*128/S, (r+1)*128/S) of the tile, every CTA sends each row's
+// partial sums to the row's owner, and the owner adds the S partials in CTA
+// order (deterministic), rounds the logits once to bf16 (the reference's
+// einsum dtype), writes them, and takes the softmax and top-k of each row
+// with one warp per token: fp32 softmax of the bf16 logits rounded to bf16
+// (the reference's softmax output dtype), the K largest probabilities in
+// descending order, equal probabilities by ascending expert id (torch.topk
+// leaves their order unspecified).  No control words, nothing allocated.
+//
+// E > 256: the logits GEMM runs on the fused layer kernel as a one-rank,
+// one-expert layer (tokens = x [T, H], weights = the router [H, E], out =
+// logits [T, E]) whose control words live in a fixed array of this file, and
+// a second kernel takes the softmax and top-k (the same arithmetic); calls of
+// this form must not overlap on the GPU, and the first one on a device looks
+// the array's address up (make it before any stream capture).
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -22,6 +31,7 @@
 
 #include "moe_ep.h"
 #include "moe_ep_internal.h"
+#include "ptx.cuh"
 
 namespace moe {
 namespace {
@@ -67,6 +77,345 @@ __device__ __forceinline__ float warp_sum(float x) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
   return x;
+}
+
+// ---------------------------------------------------------------- E <= 256: split-K cluster kernel
+constexpr int kRtThreads = 128;                 // 4 warps: TMEM lane quarters 0..3
+constexpr int kRtStages = 4;
+constexpr int kRtKB = 64;                       // K per stage (one 128-byte swizzle atom of bf16)
+constexpr int kRtTile = 128;                    // tokens per tile (MMA M)
+constexpr int kRtMaxE = 256;                    // MMA N and TMEM columns
+constexpr uint32_t kRtXBytes = kRtTile * kRtKB * 2;           // 16 KB
+constexpr uint32_t kRtAtomBytes = 64 * kRtKB * 2;             // 8 KB: 64 experts x 64 K
+constexpr uint32_t kRtStageBytes = kRtXBytes + 4 * kRtAtomBytes;  // 48 KB
+constexpr uint64_t kRtBoundNs = 2000000000ull;  // bug guard on every pipeline wait
+
+struct RouterArgs {
+  int64_t T;
+  int H, E, K, S;          // S: CTAs per cluster (split of the hidden dimension)
+  int kblocks, kb_per;     // k-blocks of the whole H, per CTA
+  int n_mma, tmem_cols, ep;  // MMA N (E rounded to 16), TMEM columns, floats per exchanged row
+  __nv_bfloat16* logits;
+  void* ids;
+  float* vals;
+  int32_t* status_host;
+};
+
+struct alignas(16) RtSmem {
+  uint64_t full[kRtStages];
+  uint64_t empty[kRtStages];
+  uint64_t acc;
+  uint64_t drain;
+  uint32_t tmem_base;
+  int err;
+  uint32_t fills[kRtStages];
+};
+
+__device__ __forceinline__ bool rt_wait(uint64_t* bar, uint32_t parity, RtSmem& sm) {
+  uint64_t deadline = 0;
+  for (uint32_t spin = 0;; ++spin) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((spin & 63) == 63) {
+      if (*reinterpret_cast<volatile int*>(&sm.err)) return false;
+      const uint64_t now = globaltimer_ns();
+      if (deadline == 0) deadline = now + kRtBoundNs;
+      else if (now > deadline) return false;
+    }
+  }
+}
+
+__device__ void rt_fail(RtSmem& sm, const RouterArgs& a, int detail) {
+  if (atomicExch(&sm.err, 1) == 0 && a.status_host)
+    *reinterpret_cast<volatile int32_t*>(a.status_host) = int32_t(status_word(kTimeout, kSitePipe, detail));
+}
+
+__device__ __forceinline__ void st_shared_cluster_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+
+// Float index of (row, col) in one source's block of the exchange buffer:
+// rows of `ep` floats, 16-byte chunks XOR-swizzled by the row so that both
+// the senders (one row per lane) and the owner's readers (one row per warp,
+// consecutive columns per lane) touch distinct banks.
+__device__ __forceinline__ int rt_xidx(int row, int col, int ep) {
+  return row * ep + ((((col >> 2) ^ (row & 7))) << 2) + (col & 3);
+}
+
+template <typename IdT>
+__global__ void __launch_bounds__(kRtThreads, 1)
+    router_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_r,
+                  const RouterArgs a) {
+  extern __shared__ unsigned char rt_dyn[];
+  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(rt_dyn) + 1023) & ~uintptr_t(1023));
+  RtSmem& sm = *reinterpret_cast<RtSmem*>(base + kRtStages * kRtStageBytes);
+  float* xbuf = reinterpret_cast<float*>(base);  // exchange buffer [S][128/S][ep], reuses the stages
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = a.S;
+  const int r = S > 1 ? int(cluster_ctarank()) : 0;
+  const int64_t m0 = int64_t(blockIdx.x / S) * kRtTile;
+  const int kb0 = r * a.kb_per;
+  const int kb1 = min(a.kblocks, kb0 + a.kb_per);
+  const int nk = max(0, kb1 - kb0);
+  const int atoms = (a.n_mma + 63) / 64;
+  const uint32_t tx = kRtXBytes + uint32_t(atoms) * kRtAtomBytes;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kRtStages; ++i) {
+      mbar_init(&sm.full[i], 1);
+      mbar_init(&sm.empty[i], 1);
+      sm.fills[i] = 0;
+    }
+    mbar_init(&sm.acc, 1);
+    mbar_init(&sm.drain, 1);
+    sm.err = 0;
+    fence_mbar_init();
+    prefetch_tensormap(&tm_x);
+    prefetch_tensormap(&tm_r);
+  }
+  if (warp == 1) {
+    __syncwarp();
+    tmem_alloc(&sm.tmem_base, uint32_t(a.tmem_cols));
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 0 && lane == 0) {
+    // TMA producer: the tile's 128 tokens and the router rows of this CTA's k-blocks.
+    for (int i = 0; i < nk; ++i) {
+      const int st = i % kRtStages;
+      if (i >= kRtStages && !rt_wait(&sm.empty[st], ((i / kRtStages) & 1) ^ 1, sm)) {
+        rt_fail(sm, a, 1);
+        break;
+      }
+      unsigned char* dst = base + st * kRtStageBytes;
+      const int kc = (kb0 + i) * kRtKB;
+      mbar_arrive_expect_tx(&sm.full[st], tx);
+      tma_load_2d(&tm_x, &sm.full[st], dst, kc, int(m0));
+      for (int at = 0; at < atoms; ++at) tma_load_2d(&tm_r, &sm.full[st], dst + kRtXBytes + at * kRtAtomBytes, at * 64, kc);
+      sm.fills[st] += 1;
+    }
+  } else if (warp == 1 && lane == 0) {
+    // MMA issuer: D[128 tokens, N] (+)= X[128, 64] . R[64, N] per stage.
+    const uint32_t idesc = make_idesc_mn(/*bf16*/ 1, kRtTile, uint32_t(a.n_mma), /*A K-major*/ 0, /*B N-major*/ 1);
+    int i = 0;
+    for (; i < nk; ++i) {
+      const int st = i % kRtStages;
+      if (!rt_wait(&sm.full[st], (i / kRtStages) & 1, sm)) {
+        rt_fail(sm, a, 2);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t xa = smem_u32(base + st * kRtStageBytes);
+      const uint32_t ra = xa + kRtXBytes;
+#pragma unroll
+      for (int k = 0; k < kRtKB / 16; ++k) {
+        const uint64_t ad = smem_desc_sw128(xa + k * 32, 16, 1024);                 // K-major: 16 K = 32 bytes
+        const uint64_t bd = smem_desc_sw128(ra + k * 2048, kRtAtomBytes, 1024);     // N-major: 16 K = 2 x 8 rows
+        tc_mma_f16(tmem, ad, bd, idesc, (i | k) != 0 ? 1u : 0u);
+      }
+      tc_commit(&sm.empty[st]);
+    }
+    tc_commit(nk > 0 && i == nk ? &sm.acc : &sm.drain);  // accumulator ready (or: every issued MMA done)
+  }
+  __syncwarp();
+
+  // This CTA's partial tile: wait for the accumulator (none without k-blocks).
+  if (nk > 0 && !rt_wait(&sm.acc, 0, sm)) rt_fail(sm, a, 3);
+  __syncthreads();
+  tc_fence_after();
+  const bool ok = nk > 0 && !*reinterpret_cast<volatile int*>(&sm.err);  // uniform over the CTA
+  // Every CTA of the cluster is done reading its stages: they become the
+  // exchange buffer.
+  if (S > 1) cluster_sync();
+
+  // Exchange: row (32*warp + lane) of the partial tile goes to its owner,
+  // into block r of the owner's buffer.
+  const int R = kRtTile / S;
+  const int row = warp * 32 + lane;
+  const int owner = row / R, lrow = row % R;
+  const uint32_t blk = smem_u32(xbuf) + uint32_t(r * R * a.ep) * 4u;
+  const uint32_t dst_blk = S > 1 ? mapa_shared(blk, uint32_t(owner)) : blk;
+  for (int c0 = 0; c0 < a.ep; c0 += 32) {
+    uint32_t v[32];
+    if (ok && c0 < a.n_mma) {
+      tmem_ld_32x32b_x32(tmem + (uint32_t(warp * 32) << 16) + uint32_t(c0), v);
+      tmem_ld_wait();
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = 0u;
+    }
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      const uint32_t addr = dst_blk + uint32_t(rt_xidx(lrow, c0 + j, a.ep)) * 4u;
+      st_shared_cluster_v4(addr, v[j], v[j + 1], v[j + 2], v[j + 3]);
+    }
+  }
+  tc_fence_before();
+  if (S > 1) cluster_sync();  // every partial has reached its owner
+  else __syncthreads();
+
+  // Owner: rows [r*R, (r+1)*R) of the tile, one warp per token.
+  const int E = a.E, K = a.K;
+  for (int lr = warp; lr < R; lr += kRtThreads / 32) {
+    const int64_t t = m0 + int64_t(r) * R + lr;
+    if (t >= a.T) break;
+    float v[8];
+    float m = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int e = lane + 32 * j;
+      float sum = 0.f;
+      if (e < E) {
+        for (int q = 0; q < S; ++q) sum += xbuf[(q * R) * a.ep + rt_xidx(lr, e, a.ep)];
+        const __nv_bfloat16 lb = __float2bfloat16_rn(sum);
+        a.logits[t * E + e] = lb;
+        v[j] = __bfloat162float(lb);
+      } else {
+        v[j] = -INFINITY;
+      }
+      m = fmaxf(m, v[j]);
+    }
+    m = warp_max(m);
+    float z = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      v[j] = (lane + 32 * j) < E ? expf(v[j] - m) : 0.f;
+      z += v[j];
+    }
+    z = warp_sum(z);
+    // Probabilities are >= 0; -1 marks a slot past E, -2 a slot already taken.
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = (lane + 32 * j) < E ? __bfloat162float(__float2bfloat16_rn(v[j] / z)) : -1.f;
+    IdT* ids = static_cast<IdT*>(a.ids);
+    for (int k = 0; k < K; ++k) {
+      float best = -3.f;
+      int be = INT_MAX;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {  // ids ascend with j: a strict > keeps the lowest id of equal values
+        if (v[j] > best) {
+          best = v[j];
+          be = lane + 32 * j;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+        if (ob > best || (ob == best && oe < be)) {
+          best = ob;
+          be = oe;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (lane + 32 * j == be) v[j] = -2.f;
+      if (lane == 0) {
+        ids[t * K + k] = static_cast<IdT>(be);
+        a.vals[t * K + k] = best;
+      }
+    }
+  }
+
+  // Teardown: after an abort, wait (bounded) for every issued load and MMA.
+  if (threadIdx.x == 0 && *reinterpret_cast<volatile int*>(&sm.err)) {
+    const uint64_t until = globaltimer_ns() + kRtBoundNs;
+    for (int st = 0; st < kRtStages; ++st) {
+      const uint32_t f = sm.fills[st];
+      if (f == 0) continue;
+      while (!mbar_try_wait(&sm.full[st], (f - 1) & 1) && globaltimer_ns() < until) {
+      }
+    }
+    while (!mbar_try_wait(&sm.drain, 0) && globaltimer_ns() < until) {
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem, uint32_t(a.tmem_cols));
+  }
+}
+
+int encode_router_maps(CUtensorMap* mx, CUtensorMap* mr, const void* x, int64_t T, int H, const void* rw, int E) {
+  const Driver& d = driver();
+  if (!d.ok) return kCudaErr;
+  {
+    cuuint64_t dims[2] = {cuuint64_t(H), cuuint64_t(T)};
+    cuuint64_t strides[1] = {cuuint64_t(H) * 2};
+    cuuint32_t box[2] = {cuuint32_t(kRtKB), cuuint32_t(kRtTile)};
+    cuuint32_t estr[2] = {1, 1};
+    if (d.cuTensorMapEncodeTiled(mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims, strides, box,
+                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return kCudaErr;
+  }
+  {
+    // Router rows [H, E], E contiguous: boxes of 64 experts x 64 K (columns
+    // past E and rows past H read as zeros).
+    cuuint64_t dims[2] = {cuuint64_t(E), cuuint64_t(H)};
+    cuuint64_t strides[1] = {cuuint64_t(E) * 2};
+    cuuint32_t box[2] = {64, cuuint32_t(kRtKB)};
+    cuuint32_t estr[2] = {1, 1};
+    if (d.cuTensorMapEncodeTiled(mr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(rw), dims, strides, box,
+                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return kCudaErr;
+  }
+  return kOk;
+}
+
+size_t router_smem_bytes() { return 1024 + size_t(kRtStages) * kRtStageBytes + sizeof(RtSmem); }
+static_assert(1024 + size_t(kRtStages) * kRtStageBytes + sizeof(RtSmem) <= 227 * 1024, "router smem plan");
+static_assert(size_t(kRtTile) * kRtMaxE * 4 <= size_t(kRtStages) * kRtStageBytes, "exchange buffer fits the stages");
+
+template <typename IdT>
+int launch_router_cluster(const void* x, int64_t T, int H, const void* rw, int E, int K, void* logits, void* ids,
+                          float* vals, int32_t* status_host, int sms, cudaStream_t s) {
+  CUtensorMap mx, mr;
+  if (encode_router_maps(&mx, &mr, x, T, H, rw, E) != kOk) return kCudaErr;
+  RouterArgs a;
+  a.T = T;
+  a.H = H;
+  a.E = E;
+  a.K = K;
+  a.kblocks = (H + kRtKB - 1) / kRtKB;
+  const int64_t tiles = (T + kRtTile - 1) / kRtTile;
+  int S = 1;
+  while (S < 8 && tiles * (S * 2) <= sms && S * 2 <= a.kblocks) S *= 2;  // fill the SMs, at most 8 per cluster
+  a.S = S;
+  a.kb_per = (a.kblocks + S - 1) / S;
+  a.n_mma = (E + 15) / 16 * 16;
+  int cols = 32;
+  while (cols < a.n_mma) cols *= 2;
+  a.tmem_cols = cols;
+  a.ep = (E + 31) / 32 * 32;
+  a.logits = static_cast<__nv_bfloat16*>(logits);
+  a.ids = ids;
+  a.vals = vals;
+  a.status_host = status_host;
+  const size_t smem = router_smem_bytes();
+  if (cudaFuncSetAttribute(router_kernel<IdT>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+    return kCudaErr;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = unsigned(S);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(unsigned(tiles * S), 1, 1);
+  cfg.blockDim = dim3(kRtThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, router_kernel<IdT>, mx, mr, a) != cudaSuccess) return kCudaErr;
+  return cudaGetLastError() == cudaSuccess ? kOk : kCudaErr;
 }
 
 // PER = probabilities held per lane (E <= 32 * PER).
@@ -153,7 +502,8 @@ int launch_topk(const __nv_bfloat16* logits, int64_t T, int E, int K, void* ids,
 using namespace moe;
 
 extern "C" int moe_router(const void* x, int64_t T, int32_t H, const void* router_w, int32_t E, int32_t K,
-                          void* logits, void* top_idxs, int32_t ids_are_int64, float* top_vals, void* stream) {
+                          void* logits, void* top_idxs, int32_t ids_are_int64, float* top_vals, int32_t* status_host,
+                          void* stream) {
   if (T < 0 || T > (int64_t(1) << 30) || H <= 0 || H % 8 || E < 8 || E % 8 || E > kMaxExperts || K < 1 ||
       K > kMaxRouteK || K > E)
     return kBadArg;
@@ -163,12 +513,18 @@ extern "C" int moe_router(const void* x, int64_t T, int32_t H, const void* route
       15)
     return kBadArg;
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return kCudaErr;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return kCudaErr;
+  if (E <= kRtMaxE)
+    return ids_are_int64 ? launch_router_cluster<long long>(x, T, H, router_w, E, K, logits, top_idxs, top_vals,
+                                                            status_host, sms, s)
+                         : launch_router_cluster<int32_t>(x, T, H, router_w, E, K, logits, top_idxs, top_vals,
+                                                          status_host, sms, s);
 
   moe_ep_layout L;
   if (workspace_layout(1, 1, H, 2, 0, 1, 0, 0, &L) != kOk) return kBadArg;
   if (kPeerTable + L.ctrl_bytes > kCountOffset) return kBadArg;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return kCudaErr;
   uint64_t base = 0;
   if (router_scratch(dev, &base) != kOk) return kCudaErr;
   // The array keeps the previous call's words: zero the control region and
@@ -197,10 +553,9 @@ extern "C" int moe_router(const void* x, int64_t T, int32_t H, const void* route
   p.max_chunks = 1;
   p.epoch = 1;
   p.timeout_ns = 1000000000ull;  // one rank: it only waits for itself
+  p.status_host = status_host;
   // One expert and few features: spread the rows over every CTA pair
   // (tiles of 16..256 rows, at least one per pair where T allows).
-  int sms = 0;
-  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return kCudaErr;
   const int64_t pairs = sms / 2 > 0 ? sms / 2 : 1;
   const int64_t feat_slices = (E + 255) / 256;
   int64_t cap = (T * feat_slices + pairs - 1) / pairs;

@@ -144,14 +144,15 @@ def recv_counts_from(counts: torch.Tensor, world_size: int, group=None) -> torch
 
 
 def router(x: torch.Tensor, router_w: torch.Tensor, topk: int, ids_dtype=torch.int64,
-           logits: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+           logits: torch.Tensor | None = None, status: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
     """The router of utils.py:17-25 on the device (``moe_router``):
     ``softmax(einsum('bh,he->be', x, router_w))`` and its top-k.
 
     x [T, H] and router_w [H, E] bf16.  Returns ``(top_vals [T, K] float32,
     top_idxs [T, K])``, probabilities descending (bf16 values), equal ones by
     ascending expert id.  ``logits`` optionally supplies the [T, E] bf16
-    scratch."""
+    buffer; ``status`` (a pinned int32 host tensor of one element) receives
+    a device-side error word, if any."""
     if x.dtype != torch.bfloat16 or router_w.dtype != torch.bfloat16:
         raise TypeError("x and router_w must be bfloat16")
     if not x.is_cuda or router_w.device != x.device:
@@ -169,7 +170,8 @@ def router(x: torch.Tensor, router_w: torch.Tensor, topk: int, ids_dtype=torch.i
     vals = torch.empty((max(T, 1), topk), dtype=torch.float32, device=x.device)
     ids = torch.empty((max(T, 1), topk), dtype=ids_dtype, device=x.device)
     N.check(N.lib().moe_router(x.data_ptr(), T, H, router_w.data_ptr(), E, topk, logits.data_ptr(), ids.data_ptr(),
-                               int(ids_dtype == torch.int64), vals.data_ptr(), _stream_ptr(x.device)), "moe_router")
+                               int(ids_dtype == torch.int64), vals.data_ptr(),
+                               None if status is None else status.data_ptr(), _stream_ptr(x.device)), "moe_router")
     return vals[:T], ids[:T]
 
 

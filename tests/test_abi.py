@@ -81,10 +81,10 @@ def test_bad_arguments_are_rejected_before_any_device_call():
     c.ret_rows, c.K = 64, 33  # K above the routing limit
     assert lib.moe_ep_run_combine(ctypes.byref(p), ctypes.byref(c), None) == N.BAD_ARG
     # router: E not a multiple of 8, K > E, H not a multiple of 8
-    assert lib.moe_router(None, 4, 64, None, 12, 2, None, None, 1, None, None) == N.BAD_ARG
-    assert lib.moe_router(None, 4, 64, None, 16, 17, None, None, 1, None, None) == N.BAD_ARG
-    assert lib.moe_router(None, 4, 60, None, 16, 2, None, None, 1, None, None) == N.BAD_ARG
-    assert lib.moe_router(None, 0, 64, None, 16, 2, None, None, 1, None, None) == N.OK  # no tokens: nothing to do
+    assert lib.moe_router(None, 4, 64, None, 12, 2, None, None, 1, None, None, None) == N.BAD_ARG
+    assert lib.moe_router(None, 4, 64, None, 16, 17, None, None, 1, None, None, None) == N.BAD_ARG
+    assert lib.moe_router(None, 4, 60, None, 16, 2, None, None, 1, None, None, None) == N.BAD_ARG
+    assert lib.moe_router(None, 0, 64, None, 16, 2, None, None, 1, None, None, None) == N.OK  # no tokens: nothing to do
 
 
 def test_status_word_decoding():

@@ -83,12 +83,15 @@ def _worker(rank, world, port, cases, q):
 
             for k, o_ in enumerate(outs):
                 check(f"call {k}", o_)
-            # dispatch placements: CTAs that only push, local tiles first
-            for pc, lf in ((8, El // 2), (2, El)):
+            # dispatch placements: CTAs that only push (loads and stores, or
+            # bulk copies), more push warps, local tiles first, senders going
+            # through destinations one at a time
+            for pc, lf, pw, pm in ((8, El // 2, 2, 0), (2, El, 2, 0), (0, El, 4, 0), (0, 0, 3, 2), (8, El, 2, 1),
+                                   (4, 0, 2, 3)):
                 for k in range(2):
-                    check(f"push_ctas={pc} local_first={lf} call {k}",
+                    check(f"push_ctas={pc} local_first={lf} push_warps={pw} push_mode={pm} call {k}",
                           apg.run(rank, coal, chunk, 1, wl.T, wl.H, wl.E, world, None, False, w.cuda(), rc,
-                                  timeout_s=10.0, push_ctas=pc, local_first=lf))
+                                  timeout_s=10.0, push_ctas=pc, local_first=lf, push_warps=pw, push_mode=pm))
             # from token rows and ids, counts exchanged inside the kernel
             for k in range(2):
                 check(f"layer call {k}", apg.layer(tok.cuda(), ids.cuda(), wl.E, w.cuda(), timeout_s=10.0,
