@@ -217,6 +217,9 @@ typedef struct moe_ep_run_params {
  * expert for every destination before the next. */
 #define MOE_EP_PUSH_BULK 1
 #define MOE_EP_PUSH_BY_DESTINATION 2
+/* HYBRID: with push CTAs, the computing CTAs' push_warps warps move rows too
+ * (all take items from one counter). */
+#define MOE_EP_PUSH_HYBRID 4
 
 /* Device timeline (globaltimer ns, or counts), one record per CTA. */
 #define MOE_EP_TRACE_WORDS 24

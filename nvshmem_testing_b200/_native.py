@@ -17,7 +17,7 @@ STATUS_NAMES = {OK: "ok", BAD_ARG: "bad argument", CUDA_ERR: "CUDA error", TIMEO
                 CAPACITY: "receive capacity exceeded", BAD_ROUTE: "bad routing input",
                 SCRATCH_LIMIT: "size exceeds the fixed scratch of moe_ep_run_noalloc"}
 NOALLOC_MAX_EXPERTS = 64
-PUSH_BULK, PUSH_BY_DESTINATION = 1, 2
+PUSH_BULK, PUSH_BY_DESTINATION, PUSH_HYBRID = 1, 2, 4
 ABI_VERSION = 3
 
 # Every symbol include/moe_ep.h declares.

@@ -63,12 +63,14 @@ def placement(W: int, El: int, push_ctas: int | None = None, local_first: int | 
 
 def push_setup(push_warps: int | None = None, push_mode: int | None = None) -> tuple[int, int]:
     """(push_warps, push_mode): warps per CTA that move rows when no push
-    CTAs are used, and the MOE_EP_PUSH_* bits (bulk copies in push CTAs,
-    destination-major order)."""
+    CTAs are used, and the MOE_EP_PUSH_* bits (1: bulk copies in push CTAs,
+    2: destination-major order, 4: computing CTAs push beside the push
+    CTAs)."""
     pw = DEFAULT_PUSH_WARPS if push_warps is None else int(push_warps)
     pm = DEFAULT_PUSH_MODE if push_mode is None else int(push_mode)
-    if not 1 <= pw <= 6 or pm & ~3:
-        raise ValueError(f"push_warps must be 1..6 and push_mode a combination of bits 1 and 2, got {pw}, {pm}")
+    if not 1 <= pw <= 6 or pm & ~7:
+        raise ValueError(f"push_warps must be 1..6 and push_mode a combination of the MOE_EP_PUSH_* bits 1, 2, 4, "
+                         f"got {pw}, {pm}")
     return pw, pm
 
 

@@ -134,6 +134,9 @@ struct Params {
   // destinations before le+1); 1 = destination-major (q = 1..W-1, destination
   // me - q, experts in order within each).
   int push_phased;
+  // With push CTAs, the computing CTAs' push_warps warps push as well
+  // (both take items from the same counter).
+  int push_hybrid;
   // Tile order: the local tiles of experts [0, local_first) come before any
   // remote tile, so the GEMM starts on rows that need no NVLink transfer.
   int local_first;
@@ -637,7 +640,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // Rows are pushed by push_warps warps of every CTA, or by the push CTAs
   // (every warp, or kBulkStreams bulk-copy streams).
-  const bool pusher = push_cta || (p.push_ctas == 0 && warp >= kWarpPush0 && warp < kWarpPush0 + p.push_warps);
+  const bool pusher = push_cta || ((p.push_ctas == 0 || p.push_hybrid) && warp >= kWarpPush0 &&
+                                   warp < kWarpPush0 + p.push_warps);
   if (run_main && !push_cta && warp == kWarpProducer) {
     if (lane == 0) {
       const uint32_t bar_leader0 = mapa_shared(smem_u32(&sm.full[0]), 0);
@@ -1003,7 +1007,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       atomicMax(&sm.push_end, static_cast<unsigned long long>(TRACE_NOW(p)));
     }
     __syncwarp();
-  } else if (run_main && p.push_ctas > 0 && !push_cta && warp >= kWarpPush0 && warp < kWarpPush0 + kZeroWarps) {
+  } else if (run_main && p.push_ctas > 0 && !p.push_hybrid && !push_cta && warp >= kWarpPush0 &&
+             warp < kWarpPush0 + kZeroWarps) {
     // With push CTAs, the computing CTAs' first push warps zero the padded
     // output rows (their own counter).
     const int np = kZeroWarps * 32;
@@ -1212,7 +1217,7 @@ int launch_fused(const moe_ep_run_params* a, const FusedMode& m, cudaStream_t st
     return kBadArg;
   if (a->num_ctas & 1u) return kBadArg;  // CTA pairs
   if (a->push_ctas < 0 || (a->push_ctas & 1) || a->local_first < 0 || a->local_first > El) return kBadArg;
-  if (a->push_warps < 0 || a->push_warps > kMaxPushWarps || (a->push_mode & ~3)) return kBadArg;
+  if (a->push_warps < 0 || a->push_warps > kMaxPushWarps || (a->push_mode & ~7)) return kBadArg;
   // Rows of the token buffer (the local TMA map's extent).
   const int64_t rows_in = m.general ? m.send_rows : int64_t(W) * El * a->gm;
   if (rows_in + kMaxTileRows > (int64_t(1) << 31) || 2 * a->cap_rows + kMaxTileRows > (int64_t(1) << 31) ||
@@ -1283,6 +1288,7 @@ int launch_fused(const moe_ep_run_params* a, const FusedMode& m, cudaStream_t st
   p.push_warps = a->push_warps > 0 ? a->push_warps : 2;
   p.push_bulk = (a->push_mode & MOE_EP_PUSH_BULK) != 0;
   p.push_phased = (a->push_mode & MOE_EP_PUSH_BY_DESTINATION) != 0;
+  p.push_hybrid = (a->push_mode & MOE_EP_PUSH_HYBRID) != 0;
   p.local_first = a->local_first;
   p.send_counts = a->counts_are_send != 0;
 

@@ -12,7 +12,7 @@
 // partial sums to the row's owner, and the owner adds the S partials in CTA
 // order (deterministic), rounds the logits once to bf16 (the reference's
 // einsum dtype), writes them, and takes the softmax and top-k of each row
-// with one warp per token: fp32 softmax of the bf16 logits rounded to bf16
+// (S threads per row): fp32 softmax of the bf16 logits rounded to bf16
 // (the reference's softmax output dtype), the K largest probabilities in
 // descending order, equal probabilities by ascending expert id (torch.topk
 // leaves their order unspecified).  No control words, nothing allocated.
@@ -80,7 +80,7 @@ __device__ __forceinline__ float warp_sum(float x) {
 }
 
 // ---------------------------------------------------------------- E <= 256: split-K cluster kernel
-constexpr int kRtThreads = 128;                 // 4 warps: TMEM lane quarters 0..3
+constexpr int kRtThreads = 512;                 // 16 warps; warp w reads TMEM lane quarter w % 4
 constexpr int kRtStages = 4;
 constexpr int kRtKB = 64;                       // K per stage (one 128-byte swizzle atom of bf16)
 constexpr int kRtTile = 128;                    // tokens per tile (MMA M)
@@ -95,6 +95,7 @@ struct RouterArgs {
   int H, E, K, S;          // S: CTAs per cluster (split of the hidden dimension)
   int kblocks, kb_per;     // k-blocks of the whole H, per CTA
   int n_mma, tmem_cols, ep;  // MMA N (E rounded to 16), TMEM columns, floats per exchanged row
+  int r3d;                   // the router map is 3-D: one box holds every 64-expert atom of a stage
   __nv_bfloat16* logits;
   void* ids;
   float* vals;
@@ -196,7 +197,12 @@ __global__ void __launch_bounds__(kRtThreads, 1)
       const int kc = (kb0 + i) * kRtKB;
       mbar_arrive_expect_tx(&sm.full[st], tx);
       tma_load_2d(&tm_x, &sm.full[st], dst, kc, int(m0));
-      for (int at = 0; at < atoms; ++at) tma_load_2d(&tm_r, &sm.full[st], dst + kRtXBytes + at * kRtAtomBytes, at * 64, kc);
+      if (a.r3d) {
+        tma_load_3d(&tm_r, &sm.full[st], dst + kRtXBytes, 0, kc, 0);
+      } else {
+        for (int at = 0; at < atoms; ++at)
+          tma_load_2d(&tm_r, &sm.full[st], dst + kRtXBytes + at * kRtAtomBytes, at * 64, kc);
+      }
       sm.fills[st] += 1;
     }
   } else if (warp == 1 && lane == 0) {
@@ -233,91 +239,95 @@ __global__ void __launch_bounds__(kRtThreads, 1)
   // exchange buffer.
   if (S > 1) cluster_sync();
 
-  // Exchange: row (32*warp + lane) of the partial tile goes to its owner,
-  // into block r of the owner's buffer.
+  // Exchange: row (32*(warp % 4) + lane) of the partial tile goes to its
+  // owner, into block r of the owner's buffer; the four warps of a lane
+  // quarter take every fourth 64-column group.
   const int R = kRtTile / S;
-  const int row = warp * 32 + lane;
+  const int quarter = warp & 3;
+  const int row = quarter * 32 + lane;
   const int owner = row / R, lrow = row % R;
   const uint32_t blk = smem_u32(xbuf) + uint32_t(r * R * a.ep) * 4u;
   const uint32_t dst_blk = S > 1 ? mapa_shared(blk, uint32_t(owner)) : blk;
-  for (int c0 = 0; c0 < a.ep; c0 += 32) {
-    uint32_t v[32];
-    if (ok && c0 < a.n_mma) {
-      tmem_ld_32x32b_x32(tmem + (uint32_t(warp * 32) << 16) + uint32_t(c0), v);
-      tmem_ld_wait();
-    } else {
+  // 64 columns per round: two TMEM loads behind one wait.
+  const uint32_t trow = tmem + (uint32_t(quarter * 32) << 16);
+  for (int c0 = (warp >> 2) * 64; c0 < a.ep; c0 += (kRtThreads / 128) * 64) {
+    uint32_t v0[32], v1[32];
+    const bool l0 = ok && c0 < a.n_mma, l1 = ok && c0 + 32 < a.n_mma;
+    if (l0) tmem_ld_32x32b_x32(trow + uint32_t(c0), v0);
+    if (l1) tmem_ld_32x32b_x32(trow + uint32_t(c0 + 32), v1);
+    if (l0 || l1) tmem_ld_wait();
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = 0u;
+    for (int j = 0; j < 32; ++j) {
+      if (!l0) v0[j] = 0u;
+      if (!l1) v1[j] = 0u;
     }
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {
-      const uint32_t addr = dst_blk + uint32_t(rt_xidx(lrow, c0 + j, a.ep)) * 4u;
-      st_shared_cluster_v4(addr, v[j], v[j + 1], v[j + 2], v[j + 3]);
+      st_shared_cluster_v4(dst_blk + uint32_t(rt_xidx(lrow, c0 + j, a.ep)) * 4u, v0[j], v0[j + 1], v0[j + 2],
+                           v0[j + 3]);
+      if (c0 + 32 < a.ep)
+        st_shared_cluster_v4(dst_blk + uint32_t(rt_xidx(lrow, c0 + 32 + j, a.ep)) * 4u, v1[j], v1[j + 1], v1[j + 2],
+                             v1[j + 3]);
     }
   }
   tc_fence_before();
   if (S > 1) cluster_sync();  // every partial has reached its owner
   else __syncthreads();
 
-  // Owner: rows [r*R, (r+1)*R) of the tile, one warp per token.
+  // Owner: rows [r*R, (r+1)*R) of the tile; TPR = kRtThreads / R
+  // neighbouring threads per row, thread `part` holding experts part,
+  // part + TPR, ...
+  // The partials are summed in CTA order, the bf16 logit written out and
+  // kept in block 0 of the buffer (then replaced by its probability); the
+  // row's max, sum and each top-k pick combine the S threads by shuffles.
   const int E = a.E, K = a.K;
-  for (int lr = warp; lr < R; lr += kRtThreads / 32) {
-    const int64_t t = m0 + int64_t(r) * R + lr;
-    if (t >= a.T) break;
-    float v[8];
-    float m = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int e = lane + 32 * j;
-      float sum = 0.f;
-      if (e < E) {
-        for (int q = 0; q < S; ++q) sum += xbuf[(q * R) * a.ep + rt_xidx(lr, e, a.ep)];
-        const __nv_bfloat16 lb = __float2bfloat16_rn(sum);
-        a.logits[t * E + e] = lb;
-        v[j] = __bfloat162float(lb);
-      } else {
-        v[j] = -INFINITY;
+  const int TPR = kRtThreads / R;  // 4 * S: 4..32, a power of two dividing 32
+  const int lr = int(threadIdx.x) / TPR, part = int(threadIdx.x) % TPR;
+  const int64_t t = m0 + int64_t(r) * R + lr;
+  const bool live = t < a.T;  // rows past T compute (zeros) but write nothing
+  float m = -INFINITY;
+  for (int e = part; e < E; e += TPR) {
+    const int xi = rt_xidx(lr, e, a.ep);
+    float sum = 0.f;
+    for (int q = 0; q < S; ++q) sum += xbuf[q * R * a.ep + xi];
+    const __nv_bfloat16 lb = __float2bfloat16_rn(sum);
+    if (live) a.logits[t * E + e] = lb;
+    const float v = __bfloat162float(lb);
+    xbuf[xi] = v;
+    m = fmaxf(m, v);
+  }
+  for (int o = 1; o < TPR; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float z = 0.f;
+  for (int e = part; e < E; e += TPR) z += expf(xbuf[rt_xidx(lr, e, a.ep)] - m);
+  for (int o = 1; o < TPR; o <<= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
+  // Probabilities are >= 0; -2 marks one already taken.
+  for (int e = part; e < E; e += TPR) {
+    const int xi = rt_xidx(lr, e, a.ep);
+    xbuf[xi] = __bfloat162float(__float2bfloat16_rn(expf(xbuf[xi] - m) / z));
+  }
+  IdT* ids = static_cast<IdT*>(a.ids);
+  for (int k = 0; k < K; ++k) {
+    float best = -3.f;
+    int be = INT_MAX;
+    for (int e = part; e < E; e += TPR) {  // ascending ids: a strict > keeps the lowest id of equal values
+      const float v = xbuf[rt_xidx(lr, e, a.ep)];
+      if (v > best) {
+        best = v;
+        be = e;
       }
-      m = fmaxf(m, v[j]);
     }
-    m = warp_max(m);
-    float z = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      v[j] = (lane + 32 * j) < E ? expf(v[j] - m) : 0.f;
-      z += v[j];
+    for (int o = 1; o < TPR; o <<= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+      if (ob > best || (ob == best && oe < be)) {
+        best = ob;
+        be = oe;
+      }
     }
-    z = warp_sum(z);
-    // Probabilities are >= 0; -1 marks a slot past E, -2 a slot already taken.
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = (lane + 32 * j) < E ? __bfloat162float(__float2bfloat16_rn(v[j] / z)) : -1.f;
-    IdT* ids = static_cast<IdT*>(a.ids);
-    for (int k = 0; k < K; ++k) {
-      float best = -3.f;
-      int be = INT_MAX;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {  // ids ascend with j: a strict > keeps the lowest id of equal values
-        if (v[j] > best) {
-          best = v[j];
-          be = lane + 32 * j;
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oe = __shfl_xor_sync(0xffffffffu, be, o);
-        if (ob > best || (ob == best && oe < be)) {
-          best = ob;
-          be = oe;
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (lane + 32 * j == be) v[j] = -2.f;
-      if (lane == 0) {
-        ids[t * K + k] = static_cast<IdT>(be);
-        a.vals[t * K + k] = best;
-      }
+    if (be % TPR == part) xbuf[rt_xidx(lr, be, a.ep)] = -2.f;
+    if (part == 0 && live) {
+      ids[t * K + k] = static_cast<IdT>(be);
+      a.vals[t * K + k] = best;
     }
   }
 
@@ -342,7 +352,8 @@ __global__ void __launch_bounds__(kRtThreads, 1)
   }
 }
 
-int encode_router_maps(CUtensorMap* mx, CUtensorMap* mr, const void* x, int64_t T, int H, const void* rw, int E) {
+int encode_router_maps(CUtensorMap* mx, CUtensorMap* mr, const void* x, int64_t T, int H, const void* rw, int E,
+                       bool r3d) {
   const Driver& d = driver();
   if (!d.ok) return kCudaErr;
   {
@@ -355,7 +366,19 @@ int encode_router_maps(CUtensorMap* mx, CUtensorMap* mr, const void* x, int64_t 
                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return kCudaErr;
   }
-  {
+  if (r3d) {
+    // Router rows [H, E] seen as (64 experts, K, E/64 atoms): one box of
+    // every atom of a 64-deep stage (few, large boxes keep more bytes in
+    // flight); rows past H read as zeros.
+    cuuint64_t dims[3] = {64, cuuint64_t(H), cuuint64_t(E / 64)};
+    cuuint64_t strides[2] = {cuuint64_t(E) * 2, 128};
+    cuuint32_t box[3] = {64, cuuint32_t(kRtKB), cuuint32_t(E / 64)};
+    cuuint32_t estr[3] = {1, 1, 1};
+    if (d.cuTensorMapEncodeTiled(mr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(rw), dims, strides, box,
+                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return kCudaErr;
+  } else {
     // Router rows [H, E], E contiguous: boxes of 64 experts x 64 K (columns
     // past E and rows past H read as zeros).
     cuuint64_t dims[2] = {cuuint64_t(E), cuuint64_t(H)};
@@ -378,8 +401,10 @@ template <typename IdT>
 int launch_router_cluster(const void* x, int64_t T, int H, const void* rw, int E, int K, void* logits, void* ids,
                           float* vals, int32_t* status_host, int sms, cudaStream_t s) {
   CUtensorMap mx, mr;
-  if (encode_router_maps(&mx, &mr, x, T, H, rw, E) != kOk) return kCudaErr;
+  const bool r3d = E % 64 == 0;
+  if (encode_router_maps(&mx, &mr, x, T, H, rw, E, r3d) != kOk) return kCudaErr;
   RouterArgs a;
+  a.r3d = r3d;
   a.T = T;
   a.H = H;
   a.E = E;

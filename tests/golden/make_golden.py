@@ -203,7 +203,7 @@ def make_layer(ref: Path) -> dict:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="directory of the reference checkout (its utils.py, baseline.py)")
     a = ap.parse_args()
     ref = Path(a.reference)
     np.savez_compressed(HERE / "routing_golden.npz", **make_routing(ref))

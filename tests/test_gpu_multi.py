@@ -87,7 +87,7 @@ def _worker(rank, world, port, cases, q):
             # bulk copies), more push warps, local tiles first, senders going
             # through destinations one at a time
             for pc, lf, pw, pm in ((8, El // 2, 2, 0), (2, El, 2, 0), (0, El, 4, 0), (0, 0, 3, 2), (8, El, 2, 1),
-                                   (4, 0, 2, 3)):
+                                   (4, 0, 2, 3), (6, El, 2, 5)):
                 for k in range(2):
                     check(f"push_ctas={pc} local_first={lf} push_warps={pw} push_mode={pm} call {k}",
                           apg.run(rank, coal, chunk, 1, wl.T, wl.H, wl.E, world, None, False, w.cuda(), rc,

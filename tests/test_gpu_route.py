@@ -87,3 +87,28 @@ def test_dispatch_matches_gen_tensor_restated(single_rank_group):
     ref, rchunk, rlen = oracle.gen_tensor_restated(tok.view(torch.int16).numpy(), ids.numpy(), wl.E, 1)
     assert chunk == rchunk and lengths == rlen
     assert np.array_equal(coal.cpu().view(torch.int16).numpy(), ref)
+
+
+def test_route_spans_every_cta_of_the_cluster():
+    """Token counts below, at and above the cluster's CTA count and chunk
+    size: each CTA routes a contiguous token range, so ranks inside a bucket
+    must continue across CTA boundaries."""
+    g = torch.Generator().manual_seed(5)
+    for T in (1, 7, 8, 9, 511, 512, 513, 4095, 4097, 40000):
+        _check(torch.randint(0, 37, (T, 3), generator=g), 37)
+        _check(torch.randint(0, 1024, (T, 2), generator=g), 1024, dtype=torch.int32)
+
+
+def test_publish_reaches_pinned_host_memory():
+    """moe_publish_i32: a device word copied by a kernel into pinned host
+    memory, read after an event (the routing's one host read)."""
+    import ctypes
+    from nvshmem_testing_b200 import _native as N
+    src = torch.tensor([7, -3, 123456], dtype=torch.int32, device="cuda")
+    host = torch.zeros(3, dtype=torch.int32, pin_memory=True)
+    N.check(N.lib().moe_publish_i32(src.data_ptr(), 3, host.data_ptr(),
+                                    ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)), "moe_publish_i32")
+    ev = torch.cuda.Event()
+    ev.record()
+    ev.synchronize()
+    assert host.tolist() == [7, -3, 123456]
