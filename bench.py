@@ -747,7 +747,7 @@ def run_router_path(args) -> int:
                          "roofline_us": t_roof * 1e6, "frac": t_roof / (ms * 1e-3),
                          "frac_graph": t_roof / (ms_g * 1e-3), "peak_source": src,
                          "flops": flops, "algorithmic_hbm_bytes": hbm},
-            "gpu_launches": 3 * args.steps,  # count word, logits GEMM, softmax/top-k
+            "gpu_launches": args.steps * (1 if wl.E <= 256 else 3),  # one router kernel (E <= 256)
             "clocks": clocks}
     if rank == 0:
         print(json.dumps(line), flush=True)
