@@ -72,14 +72,15 @@ int moe_ep_num_sms(int device, int* out);
  *   offsets   [E+1]  exclusive scan of counts
  *   perm      [T*K]  perm[offsets[e] + j] = j-th token (ascending) of expert e
  *   max_count [1]    max over e of counts[e] (utils.py:45, local max)
- * E <= 1024, K <= 32.  One CTA; suited to T up to ~10^5 tokens. */
+ * E <= 1024, K <= 32.  One cluster of 8 CTAs, each routing a contiguous
+ * token range; they find their bucket offsets from each other's counts
+ * through distributed shared memory (no scratch memory). */
 int moe_route(const void* top_idxs, int ids_are_int64, int64_t T, int K, int E, int32_t* counts, int32_t* offsets,
               int32_t* perm, int32_t* max_count, void* stream);
 
 /* Replaces the router of utils.py:17-25 (the step before the path):
  *   logits [T, E] bf16 = x [T, H] @ router_w [H, E]   (bf16 in, fp32
- *                        accumulation rounded once: the tcgen05 GEMM of
- *                        moe_ep_run as a one-rank, one-expert layer)
+ *                        accumulation rounded once to bf16)
  *   probs              = softmax over E in fp32, rounded to bf16
  *   top_idxs [T, K]    = the K most probable experts, descending, equal
  *                        probabilities by ascending id (int64 or int32)
@@ -207,8 +208,14 @@ typedef struct moe_ep_run_params {
   int32_t push_warps;          /* push_ctas == 0: warps of every CTA that move rows */
                                /* (1..6; 0 = 2)                                     */
   int32_t push_mode;           /* MOE_EP_PUSH_* bits                                */
-  int32_t reserved0;           /* 0                                                 */
+  int32_t sched_mode;          /* MOE_EP_SCHED_* bits (0: one fixed tile order)     */
 } moe_ep_run_params;
+
+/* sched_mode bits.  READY_FIRST (more than one rank): a CTA pair takes the
+ * next remote tile when every row it reads has landed and a local tile
+ * otherwise (local tiles from their own counter), so that local work fills
+ * the waits for rows in flight; local_first is then ignored. */
+#define MOE_EP_SCHED_READY_FIRST 1
 
 /* push_mode bits.  BULK: push CTAs move rows with TMA bulk copies (local rows
  * through a ring of shared-memory pieces to the peer) instead of loads and

@@ -18,6 +18,7 @@ STATUS_NAMES = {OK: "ok", BAD_ARG: "bad argument", CUDA_ERR: "CUDA error", TIMEO
                 SCRATCH_LIMIT: "size exceeds the fixed scratch of moe_ep_run_noalloc"}
 NOALLOC_MAX_EXPERTS = 64
 PUSH_BULK, PUSH_BY_DESTINATION, PUSH_HYBRID = 1, 2, 4
+SCHED_READY_FIRST = 1
 ABI_VERSION = 3
 
 # Every symbol include/moe_ep.h declares.
@@ -54,7 +55,7 @@ class RunParams(ctypes.Structure):
                 ("timeout_ns", ctypes.c_uint64), ("status_host", ctypes.c_void_p), ("trace", ctypes.c_void_p),
                 ("push_ctas", ctypes.c_int32), ("local_first", ctypes.c_int32),
                 ("counts_are_send", ctypes.c_int32), ("push_warps", ctypes.c_int32), ("push_mode", ctypes.c_int32),
-                ("reserved0", ctypes.c_int32)]
+                ("sched_mode", ctypes.c_int32)]
 
 
 class CombineParams(ctypes.Structure):

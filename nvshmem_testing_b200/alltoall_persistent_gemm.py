@@ -46,6 +46,7 @@ DEFAULT_PUSH_CTAS = int(os.environ.get("MOE_EP_PUSH_CTAS", "0"))
 DEFAULT_LOCAL_FIRST = int(os.environ.get("MOE_EP_LOCAL_FIRST", "0"))
 DEFAULT_PUSH_WARPS = int(os.environ.get("MOE_EP_PUSH_WARPS", "2"))
 DEFAULT_PUSH_MODE = int(os.environ.get("MOE_EP_PUSH_MODE", "0"))
+DEFAULT_READY_FIRST = os.environ.get("MOE_EP_READY_FIRST", "0") not in ("", "0")
 
 
 def placement(W: int, El: int, push_ctas: int | None = None, local_first: int | None = None) -> tuple[int, int]:
@@ -92,7 +93,7 @@ def _launch_params(me: int, W: int, tokens: torch.Tensor, gm: int | None, transm
                    local_weights: torch.Tensor, recv_counts, group, timeout_s, push_rows, num_ctas, trace,
                    ret_cols: int = 0, push_ctas: int | None = None, local_first: int | None = None,
                    send_counts: torch.Tensor | None = None, push_warps: int | None = None,
-                   push_mode: int | None = None):
+                   push_mode: int | None = None, ready_first: bool | None = None):
     """Validate the fused layer's inputs and fill ``moe_ep_run_params``.
 
     ``gm`` is the bound on every (rank, expert) count; ``None`` means the
@@ -143,6 +144,8 @@ def _launch_params(me: int, W: int, tokens: torch.Tensor, gm: int | None, transm
     p.num_ctas = num_ctas
     p.push_ctas, p.local_first = placement(W, El, push_ctas, local_first)
     p.push_warps, p.push_mode = push_setup(push_warps, push_mode)
+    rf = DEFAULT_READY_FIRST if ready_first is None else bool(ready_first)
+    p.sched_mode = N.SCHED_READY_FIRST if (rf and W > 1) else 0
     p.counts_are_send = int(send_counts is not None)
     p.timeout_ns = int((timeout_s if timeout_s is not None else DEFAULT_TIMEOUT_S) * 1e9)
     p.status_host = ws.status_host.data_ptr()
@@ -173,7 +176,7 @@ def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: in
         check: bool = False, trace: torch.Tensor | None = None, max_count: int | None = None,
         recv_rows: int | None = None, push_ctas: int | None = None, local_first: int | None = None,
         send_counts: torch.Tensor | None = None, push_warps: int | None = None,
-        push_mode: int | None = None) -> torch.Tensor:
+        push_mode: int | None = None, ready_first: bool | None = None) -> torch.Tensor:
     """Fused dispatch + grouped GEMM; see the module docstring.
 
     ``general_a2a=True`` (a stub in the reference, alltoall_persistent_gemm.py:221-222)
@@ -196,6 +199,8 @@ def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: in
     receives the per-CTA device timeline, ``_native.TRACE_FIELDS``),
     ``push_ctas`` / ``local_first`` (dispatch placement, see ``placement``),
     ``push_warps`` / ``push_mode`` (how rows move, see ``push_setup``),
+    ``ready_first`` (more than one rank: remote tiles whose rows have landed
+    first, local tiles while none has; ``local_first`` is then ignored),
     ``send_counts`` (padded path only: this rank's ``[W*El]`` per-expert
     counts, i.e. the routing's ``lengths``, in place of ``recv_counts``; the
     kernel's count exchange then replaces the count all-to-all of
@@ -223,7 +228,8 @@ def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: in
         ws, p, (El, gm, Nout), keep = _launch_params(me, W, tokens, gm, transmit_size, hidden_dim, local_weights,
                                                      recv_counts, group, timeout_s, push_rows, num_ctas, trace,
                                                      push_ctas=push_ctas, local_first=local_first,
-                                                     push_warps=push_warps, push_mode=push_mode)
+                                                     push_warps=push_warps, push_mode=push_mode,
+                                                     ready_first=ready_first)
         # A zero-row view has a null data_ptr; the kernel wants a real buffer.
         buf = torch.empty((max(out_rows, 1), Nout), dtype=torch.bfloat16, device=tokens.device)
         out = buf[:out_rows]
@@ -237,7 +243,7 @@ def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: in
                                                      recv_counts, group, timeout_s, push_rows, num_ctas, trace,
                                                      push_ctas=push_ctas, local_first=local_first,
                                                      send_counts=send_counts, push_warps=push_warps,
-                                                     push_mode=push_mode)
+                                                     push_mode=push_mode, ready_first=ready_first)
         out = torch.empty((El, W * gm, Nout), dtype=torch.bfloat16, device=tokens.device)
         p.out = out.data_ptr()
         stream = torch.cuda.current_stream(tokens.device)

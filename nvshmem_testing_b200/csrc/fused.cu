@@ -140,6 +140,10 @@ struct Params {
   // Tile order: the local tiles of experts [0, local_first) come before any
   // remote tile, so the GEMM starts on rows that need no NVLink transfer.
   int local_first;
+  // Ready-first scheduling (local_first = El): a leader takes the next
+  // remote tile if every row chunk it reads has landed, otherwise a local
+  // tile from a second counter, so local work fills the waits for NVLink.
+  int ready_first;
   // recv_counts holds this rank's send counts [W dst][El] instead of its
   // receive counts [W src][El]; every rank publishes its block either way,
   // so the exchanged matrix is read transposed and no host-side count
@@ -331,6 +335,24 @@ __device__ __forceinline__ Tile decode_tile(const Sched& s, int W, int El, int m
   tl.row1 = min(tl.row0 + tr, rows);
   tl.n = (tl.row1 - tl.row0 + 15) & ~15;
   return tl;
+}
+
+// Ready-first: whether every row chunk a remote tile reads has landed (one
+// acquire load per chunk, no waiting).
+__device__ bool tile_rows_landed(const Params& p, const Sched& s, const Tile& tl) {
+  const int W = p.W, El = p.El;
+  const uint32_t par = p.epoch & 1u;
+  const int* sg = s.seg + tl.le * (W + 1);
+  for (int q = 1; q < W; ++q) {
+    const int lo = max(tl.row0, sg[q]), hi = min(tl.row1, sg[q + 1]);
+    if (lo >= hi) continue;
+    const int src = (p.me + q) % W;
+    const uint32_t* fl =
+        reinterpret_cast<const uint32_t*>(p.local + p.off_dflag) + ((size_t(par) * W + src) * El + tl.le) * p.max_chunks;
+    for (int c = (lo - sg[q]) / p.push_rows; c <= (hi - 1 - sg[q]) / p.push_rows; ++c)
+      if (int32_t(ld_acquire_sys(fl + c) - p.epoch) < 0) return false;
+  }
+  return true;
 }
 
 // Rows per tile for `rows` rows: the fewest tiles of at most `cap` rows
@@ -649,14 +671,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint64_t flag_ns = 0, empty_ns = 0;
       // The leader claims one tile ahead, so the counter's round trip
       // overlaps the current tile's loads.
-      int claimed = leader ? int(atomicAdd(&lw->tile_ctr[par], 1u)) : -1;
+      // Ready-first: local tiles [0, nloc), remote tiles [nloc, tiles_total)
+      // from separate counters; `claimed` is then the pending remote tile.
+      const int nloc = s.lf_pfx[p.local_first];
+      auto claim_remote = [&]() {
+        const int r = int(atomicAdd(&lw->tile_ctr[par], 1u));
+        return r < s.tiles_total - nloc ? nloc + r : s.tiles_total;
+      };
+      int claimed = !leader ? -1 : p.ready_first ? claim_remote() : int(atomicAdd(&lw->tile_ctr[par], 1u));
       for (;; ++ti) {
         const int slot = int(ti % kGoSlots);
         int t;
         Tile tl{};
         if (leader) {
-          t = (aborted(sm) || claimed >= s.tiles_total) ? -1 : claimed;
-          if (t >= 0) claimed = int(atomicAdd(&lw->tile_ctr[par], 1u));
+          if (p.ready_first) {
+            t = -1;
+            if (!aborted(sm)) {
+              if (claimed < s.tiles_total) {
+                if (tile_rows_landed(p, s, decode_tile(s, W, El, me, p.local_first, claimed))) {
+                  t = claimed;
+                  claimed = claim_remote();
+                } else {
+                  const int l = int(atomicAdd(&lw->local_ctr[par], 1u));
+                  if (l < nloc) {
+                    t = l;
+                  } else {  // no local work left: wait for the pending tile's rows
+                    t = claimed;
+                    claimed = claim_remote();
+                  }
+                }
+              } else {
+                const int l = int(atomicAdd(&lw->local_ctr[par], 1u));
+                t = l < nloc ? l : -1;
+              }
+            }
+          } else {
+            t = (aborted(sm) || claimed >= s.tiles_total) ? -1 : claimed;
+            if (t >= 0) claimed = int(atomicAdd(&lw->tile_ctr[par], 1u));
+          }
           bool ok = t >= 0;
           if (ok) tl = decode_tile(s, W, El, me, p.local_first, t);
           const uint64_t tw0 = TRACE_NOW(p);
@@ -1080,6 +1132,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       else __threadfence();
       lw->push_ctr[par ^ 1] = 0;
       lw->zero_ctr[par ^ 1] = 0;
+      lw->local_ctr[par ^ 1] = 0;
       lw->tile_ctr[par ^ 1] = 0;
       lw->done_ctr[par ^ 1] = 0;
       __threadfence();
@@ -1217,7 +1270,8 @@ int launch_fused(const moe_ep_run_params* a, const FusedMode& m, cudaStream_t st
     return kBadArg;
   if (a->num_ctas & 1u) return kBadArg;  // CTA pairs
   if (a->push_ctas < 0 || (a->push_ctas & 1) || a->local_first < 0 || a->local_first > El) return kBadArg;
-  if (a->push_warps < 0 || a->push_warps > kMaxPushWarps || (a->push_mode & ~7)) return kBadArg;
+  if (a->push_warps < 0 || a->push_warps > kMaxPushWarps || (a->push_mode & ~7) || (a->sched_mode & ~1))
+    return kBadArg;
   // Rows of the token buffer (the local TMA map's extent).
   const int64_t rows_in = m.general ? m.send_rows : int64_t(W) * El * a->gm;
   if (rows_in + kMaxTileRows > (int64_t(1) << 31) || 2 * a->cap_rows + kMaxTileRows > (int64_t(1) << 31) ||
@@ -1289,7 +1343,8 @@ int launch_fused(const moe_ep_run_params* a, const FusedMode& m, cudaStream_t st
   p.push_bulk = (a->push_mode & MOE_EP_PUSH_BULK) != 0;
   p.push_phased = (a->push_mode & MOE_EP_PUSH_BY_DESTINATION) != 0;
   p.push_hybrid = (a->push_mode & MOE_EP_PUSH_HYBRID) != 0;
-  p.local_first = a->local_first;
+  p.ready_first = (a->sched_mode & MOE_EP_SCHED_READY_FIRST) != 0 && W > 1;
+  p.local_first = p.ready_first ? El : a->local_first;
   p.send_counts = a->counts_are_send != 0;
 
   const size_t smem = fused_smem_bytes();

@@ -46,6 +46,7 @@ struct LocalWords {
   uint32_t tile_ctr[2];
   uint32_t pad;
   uint32_t zero_ctr[2];
+  uint32_t local_ctr[2];
 };
 
 int launch_publish_i32(const int32_t* src, int64_t n, int32_t* dst, cudaStream_t stream);

@@ -86,12 +86,14 @@ def _worker(rank, world, port, cases, q):
             # dispatch placements: CTAs that only push (loads and stores, or
             # bulk copies), more push warps, local tiles first, senders going
             # through destinations one at a time
-            for pc, lf, pw, pm in ((8, El // 2, 2, 0), (2, El, 2, 0), (0, El, 4, 0), (0, 0, 3, 2), (8, El, 2, 1),
-                                   (4, 0, 2, 3), (6, El, 2, 5)):
+            for pc, lf, pw, pm, rf in ((8, El // 2, 2, 0, 0), (2, El, 2, 0, 0), (0, El, 4, 0, 0), (0, 0, 3, 2, 0),
+                                       (8, El, 2, 1, 0), (4, 0, 2, 3, 0), (6, El, 2, 5, 0), (0, 0, 2, 0, 1),
+                                       (0, 0, 4, 2, 1)):
                 for k in range(2):
-                    check(f"push_ctas={pc} local_first={lf} push_warps={pw} push_mode={pm} call {k}",
+                    check(f"push_ctas={pc} local_first={lf} push_warps={pw} push_mode={pm} ready_first={rf} call {k}",
                           apg.run(rank, coal, chunk, 1, wl.T, wl.H, wl.E, world, None, False, w.cuda(), rc,
-                                  timeout_s=10.0, push_ctas=pc, local_first=lf, push_warps=pw, push_mode=pm))
+                                  timeout_s=10.0, push_ctas=pc, local_first=lf, push_warps=pw, push_mode=pm,
+                                  ready_first=bool(rf)))
             # from token rows and ids, counts exchanged inside the kernel
             for k in range(2):
                 check(f"layer call {k}", apg.layer(tok.cuda(), ids.cuda(), wl.E, w.cuda(), timeout_s=10.0,
