@@ -1125,6 +1125,7 @@ def main(argv=None) -> int:
                    "parallelism": f"ep{world}", "l2": "inputs larger than L2 (weights and tokens > 126 MB)",
                    "push_ctas": apg.placement(world, case.El)[0], "local_first": apg.placement(world, case.El)[1],
                    "push_warps": apg.push_setup()[0], "push_mode": apg.push_setup()[1],
+                   "ready_first": apg.DEFAULT_READY_FIRST and world > 1, "merged": apg.DEFAULT_MERGED and world > 1,
                    "push_rows": apg.DEFAULT_PUSH_ROWS},
         "parity_vs_nccl_allclose": head["parity_vs_nccl_allclose"],
         "parity_oracle": parity,

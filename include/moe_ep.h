@@ -216,6 +216,11 @@ typedef struct moe_ep_run_params {
  * otherwise (local tiles from their own counter), so that local work fills
  * the waits for rows in flight; local_first is then ignored. */
 #define MOE_EP_SCHED_READY_FIRST 1
+/* MERGED (more than one rank; overrides READY_FIRST and local_first): an
+ * expert's local and remote rows are cut into tiles together (local rows,
+ * padded to 8, then remote rows), so each weight slice is streamed by as few
+ * tiles as the expert's rows need. */
+#define MOE_EP_SCHED_MERGED 2
 
 /* push_mode bits.  BULK: push CTAs move rows with TMA bulk copies (local rows
  * through a ring of shared-memory pieces to the peer) instead of loads and

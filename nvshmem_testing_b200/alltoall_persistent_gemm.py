@@ -47,6 +47,7 @@ DEFAULT_LOCAL_FIRST = int(os.environ.get("MOE_EP_LOCAL_FIRST", "0"))
 DEFAULT_PUSH_WARPS = int(os.environ.get("MOE_EP_PUSH_WARPS", "2"))
 DEFAULT_PUSH_MODE = int(os.environ.get("MOE_EP_PUSH_MODE", "0"))
 DEFAULT_READY_FIRST = os.environ.get("MOE_EP_READY_FIRST", "0") not in ("", "0")
+DEFAULT_MERGED = os.environ.get("MOE_EP_MERGED", "0") not in ("", "0")
 
 
 def placement(W: int, El: int, push_ctas: int | None = None, local_first: int | None = None) -> tuple[int, int]:
@@ -93,7 +94,7 @@ def _launch_params(me: int, W: int, tokens: torch.Tensor, gm: int | None, transm
                    local_weights: torch.Tensor, recv_counts, group, timeout_s, push_rows, num_ctas, trace,
                    ret_cols: int = 0, push_ctas: int | None = None, local_first: int | None = None,
                    send_counts: torch.Tensor | None = None, push_warps: int | None = None,
-                   push_mode: int | None = None, ready_first: bool | None = None):
+                   push_mode: int | None = None, ready_first: bool | None = None, merged: bool | None = None):
     """Validate the fused layer's inputs and fill ``moe_ep_run_params``.
 
     ``gm`` is the bound on every (rank, expert) count; ``None`` means the
@@ -145,7 +146,8 @@ def _launch_params(me: int, W: int, tokens: torch.Tensor, gm: int | None, transm
     p.push_ctas, p.local_first = placement(W, El, push_ctas, local_first)
     p.push_warps, p.push_mode = push_setup(push_warps, push_mode)
     rf = DEFAULT_READY_FIRST if ready_first is None else bool(ready_first)
-    p.sched_mode = N.SCHED_READY_FIRST if (rf and W > 1) else 0
+    mg = DEFAULT_MERGED if merged is None else bool(merged)
+    p.sched_mode = (N.SCHED_READY_FIRST if (rf and W > 1) else 0) | (N.SCHED_MERGED if (mg and W > 1) else 0)
     p.counts_are_send = int(send_counts is not None)
     p.timeout_ns = int((timeout_s if timeout_s is not None else DEFAULT_TIMEOUT_S) * 1e9)
     p.status_host = ws.status_host.data_ptr()
@@ -176,7 +178,7 @@ def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: in
         check: bool = False, trace: torch.Tensor | None = None, max_count: int | None = None,
         recv_rows: int | None = None, push_ctas: int | None = None, local_first: int | None = None,
         send_counts: torch.Tensor | None = None, push_warps: int | None = None,
-        push_mode: int | None = None, ready_first: bool | None = None) -> torch.Tensor:
+        push_mode: int | None = None, ready_first: bool | None = None, merged: bool | None = None) -> torch.Tensor:
     """Fused dispatch + grouped GEMM; see the module docstring.
 
     ``general_a2a=True`` (a stub in the reference, alltoall_persistent_gemm.py:221-222)
@@ -201,6 +203,9 @@ def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: in
     ``push_warps`` / ``push_mode`` (how rows move, see ``push_setup``),
     ``ready_first`` (more than one rank: remote tiles whose rows have landed
     first, local tiles while none has; ``local_first`` is then ignored),
+    ``merged`` (more than one rank: an expert's local and remote rows cut
+    into tiles together, so each weight slice is streamed by fewer tiles;
+    overrides ``ready_first`` and ``local_first``),
     ``send_counts`` (padded path only: this rank's ``[W*El]`` per-expert
     counts, i.e. the routing's ``lengths``, in place of ``recv_counts``; the
     kernel's count exchange then replaces the count all-to-all of
@@ -229,7 +234,7 @@ def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: in
                                                      recv_counts, group, timeout_s, push_rows, num_ctas, trace,
                                                      push_ctas=push_ctas, local_first=local_first,
                                                      push_warps=push_warps, push_mode=push_mode,
-                                                     ready_first=ready_first)
+                                                     ready_first=ready_first, merged=merged)
         # A zero-row view has a null data_ptr; the kernel wants a real buffer.
         buf = torch.empty((max(out_rows, 1), Nout), dtype=torch.bfloat16, device=tokens.device)
         out = buf[:out_rows]
@@ -243,7 +248,8 @@ def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: in
                                                      recv_counts, group, timeout_s, push_rows, num_ctas, trace,
                                                      push_ctas=push_ctas, local_first=local_first,
                                                      send_counts=send_counts, push_warps=push_warps,
-                                                     push_mode=push_mode, ready_first=ready_first)
+                                                     push_mode=push_mode, ready_first=ready_first,
+                                                     merged=merged)
         out = torch.empty((El, W * gm, Nout), dtype=torch.bfloat16, device=tokens.device)
         p.out = out.data_ptr()
         stream = torch.cuda.current_stream(tokens.device)

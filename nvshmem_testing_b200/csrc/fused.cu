@@ -144,6 +144,12 @@ struct Params {
   // remote tile if every row chunk it reads has landed, otherwise a local
   // tile from a second counter, so local work fills the waits for NVLink.
   int ready_first;
+  // Merged tiles: an expert's local rows and its remote rows form one row
+  // space (local rows, padded to 8, then remote rows), cut into tiles
+  // together, so that each weight slice is read by as few tiles as the rows
+  // need (one, where local + remote rows fit 256) instead of separate local
+  // and remote tiles.  local_first and ready_first are then off.
+  int merged;
   // recv_counts holds this rank's send counts [W dst][El] instead of its
   // receive counts [W src][El]; every rank publishes its block either way,
   // so the exchanged matrix is read transposed and no host-side count
@@ -301,7 +307,24 @@ struct Tile {
   int le, feat, remote;
   int row0, row1;  // rows [row0, row1) of the expert's local slot or compact remote rows
   int n;           // MMA N: row1 - row0 rounded up to 16
+  // Merged tiles: rows [row0, row1) of the expert's merged row space; rows
+  // below lr are local, [lr, lr8) padding (computed, never stored), rows
+  // from lr8 on are remote row (row - lr8).  remote: the tile holds remote rows.
+  int merged, lr, lr8;
 };
+
+// The remote rows [lo, hi) a tile reads (empty when hi <= lo).
+__device__ __forceinline__ void tile_remote_rows(const Tile& tl, int& lo, int& hi) {
+  if (tl.merged) {
+    lo = max(tl.row0, tl.lr8) - tl.lr8;
+    hi = tl.row1 - tl.lr8;
+  } else if (tl.remote) {
+    lo = tl.row0;
+    hi = tl.row1;
+  } else {
+    lo = hi = 0;
+  }
+}
 
 // Tiles are expert-major: expert le's cell holds nfeat feature slices, each
 // followed by all of its row tiles (local first, then remote), so the tiles
@@ -309,7 +332,24 @@ struct Tile {
 // read it once from HBM.  With local_first = X > 0 the local tiles of
 // experts [0, X) come first of all (same order among themselves), and those
 // experts' cells then hold only their remote tiles.
-__device__ __forceinline__ Tile decode_tile(const Sched& s, int W, int El, int me, int lf, int t) {
+__device__ __forceinline__ Tile decode_tile(const Sched& s, int W, int El, int me, int lf, int t, bool merged) {
+  if (merged) {  // one row space per expert: local rows, padding to 8, remote rows
+    const int c = find_cell(s.tile_pfx, El, t);
+    const int r = t - s.tile_pfx[c];
+    Tile tl;
+    tl.le = c;
+    tl.merged = 1;
+    tl.feat = r / s.loc_nt[c];
+    const int i = r % s.loc_nt[c];
+    const int run = s.seg[c * (W + 1) + W];
+    tl.lr = s.cnt[me * El + c];
+    tl.lr8 = run > 0 ? (tl.lr + 7) & ~7 : tl.lr;
+    tl.row0 = i * s.loc_tr[c];
+    tl.row1 = min(tl.row0 + s.loc_tr[c], tl.lr8 + run);
+    tl.remote = tl.row1 > tl.lr8;
+    tl.n = (tl.row1 - tl.row0 + 15) & ~15;
+    return tl;
+  }
   const int lf_total = s.lf_pfx[lf];
   int c, r, lnt, nrt;
   if (t < lf_total) {
@@ -325,6 +365,8 @@ __device__ __forceinline__ Tile decode_tile(const Sched& s, int W, int El, int m
   }
   Tile tl;
   tl.le = c;
+  tl.merged = 0;
+  tl.lr = tl.lr8 = 0;
   tl.feat = r / nrt;
   int i = r % nrt;
   tl.remote = i >= lnt;
@@ -343,8 +385,10 @@ __device__ bool tile_rows_landed(const Params& p, const Sched& s, const Tile& tl
   const int W = p.W, El = p.El;
   const uint32_t par = p.epoch & 1u;
   const int* sg = s.seg + tl.le * (W + 1);
-  for (int q = 1; q < W; ++q) {
-    const int lo = max(tl.row0, sg[q]), hi = min(tl.row1, sg[q + 1]);
+  int rlo, rhi;
+  tile_remote_rows(tl, rlo, rhi);
+  for (int q = 1; q < W && rlo < rhi; ++q) {
+    const int lo = max(rlo, sg[q]), hi = min(rhi, sg[q + 1]);
     if (lo >= hi) continue;
     const int src = (p.me + q) % W;
     const uint32_t* fl =
@@ -449,10 +493,18 @@ __device__ void build_schedule(const Params& p, Sched& s, Smem& sm) {
     }
     sg[W] = run;
     const int lr = s.cnt[me * El + le];
-    s.loc_tr[le] = tile_rows(lr, p.tile_cap);
-    s.rem_tr[le] = tile_rows(run, p.tile_cap);
-    s.loc_nt[le] = (lr + s.loc_tr[le] - 1) / s.loc_tr[le];
-    s.rem_nt[le] = (run + s.rem_tr[le] - 1) / s.rem_tr[le];
+    if (p.merged) {  // one row space: local rows, padding to 8, remote rows
+      const int v = run > 0 ? ((lr + 7) & ~7) + run : lr;
+      s.loc_tr[le] = tile_rows(v, p.tile_cap);
+      s.loc_nt[le] = (v + s.loc_tr[le] - 1) / s.loc_tr[le];
+      s.rem_tr[le] = 16;
+      s.rem_nt[le] = 0;
+    } else {
+      s.loc_tr[le] = tile_rows(lr, p.tile_cap);
+      s.rem_tr[le] = tile_rows(run, p.tile_cap);
+      s.loc_nt[le] = (lr + s.loc_tr[le] - 1) / s.loc_tr[le];
+      s.rem_nt[le] = (run + s.rem_tr[le] - 1) / s.rem_tr[le];
+    }
     s.rbase[le] = run;                                   // scanned below
     const bool lf = le < p.local_first;
     s.tile_pfx[le] = ((lf ? 0 : s.loc_nt[le]) + s.rem_nt[le]) * nfeat;  // scanned below
@@ -688,7 +740,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             t = -1;
             if (!aborted(sm)) {
               if (claimed < s.tiles_total) {
-                if (tile_rows_landed(p, s, decode_tile(s, W, El, me, p.local_first, claimed))) {
+                if (tile_rows_landed(p, s, decode_tile(s, W, El, me, p.local_first, claimed, p.merged))) {
                   t = claimed;
                   claimed = claim_remote();
                 } else {
@@ -710,12 +762,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (t >= 0) claimed = int(atomicAdd(&lw->tile_ctr[par], 1u));
           }
           bool ok = t >= 0;
-          if (ok) tl = decode_tile(s, W, El, me, p.local_first, t);
+          if (ok) tl = decode_tile(s, W, El, me, p.local_first, t, p.merged);
           const uint64_t tw0 = TRACE_NOW(p);
           if (ok && tl.remote) {
             const int* sg = s.seg + tl.le * (W + 1);
+            int rlo, rhi;
+            tile_remote_rows(tl, rlo, rhi);
             for (int q = 1; q < W && ok; ++q) {
-              const int lo = max(tl.row0, sg[q]), hi = min(tl.row1, sg[q + 1]);
+              const int lo = max(rlo, sg[q]), hi = min(rhi, sg[q + 1]);
               if (lo >= hi) continue;
               const int src = (me + q) % W;
               const uint32_t* fl = at_u32(p.local, p.off_dflag) + ((size_t(par) * W + src) * El + tl.le) * p.max_chunks;
@@ -738,7 +792,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
           t = wait_tile(sm, ti, pipe_bound);
           if (t < 0) break;
-          tl = decode_tile(s, W, El, me, p.local_first, t);
+          tl = decode_tile(s, W, El, me, p.local_first, t, p.merged);
         }
         if (tl.remote) fence_proxy_async_global();
         const int half = tl.n >> 1;
@@ -752,10 +806,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int nb_mine = max(0, min(2, (p.N - f_mine + 63) / 64));
         const int nb_peer = max(0, min(2, (p.N - f_peer + 63) / 64));
         // Rows go in one box of the smallest height >= half (rows past the
-        // tile land in unused shared memory).
+        // tile land in unused shared memory).  A merged tile's half is one
+        // or two segments (local rows from the send buffer, remote rows from
+        // the receive region), each 8-row aligned and loaded as exact
+        // power-of-two boxes so that neither overwrites the other.
         int bm = 0;
         while ((8 << bm) < half) ++bm;
-        const uint32_t b_bytes = 2 * uint32_t(8 << bm) * BK * 2;  // two 64-K halves
+        const uint32_t b_bytes = tl.merged ? 2 * uint32_t(half) * BK * 2 : 2 * uint32_t(8 << bm) * BK * 2;
+        int nseg = 0;
+        int64_t seg_row[2];
+        int seg_off[2], seg_len[2], seg_rem[2];
+        if (tl.merged) {
+          const int h0 = tl.row0 + int(crank) * half, h1 = h0 + half;
+          if (h0 < tl.lr8) {
+            seg_row[nseg] = local_cell + h0;
+            seg_off[nseg] = 0;
+            seg_len[nseg] = min(h1, tl.lr8) - h0;
+            seg_rem[nseg++] = 0;
+          }
+          if (h1 > tl.lr8) {
+            const int v0 = max(h0, tl.lr8);
+            seg_row[nseg] = int64_t(par) * p.cap_rows + s.rbase[tl.le] + (v0 - tl.lr8);
+            seg_off[nseg] = v0 - h0;
+            seg_len[nseg] = h1 - v0;
+            seg_rem[nseg++] = 1;
+          }
+        }
         const uint32_t tx = uint32_t(nb_mine + nb_peer) * kABox + 2 * b_bytes;
         bool stop = false;
         // With k staggering, tile t starts its K loop at k-block t % kblocks
@@ -785,8 +861,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < nb_mine; ++j)
               tma_load_3d_pair(&tm_w, bar, a_dst + j * kABox, f_mine + 64 * j, kc * KB, tl.le);
           }
-          tma_load_2d_pair(&rm.m[bm], bar, b_dst, kc * KB, int(row_base));
-          tma_load_2d_pair(&rm.m[bm], bar, b_dst + kBHalf, kc * KB + BK, int(row_base));
+          if (tl.merged) {
+            for (int g = 0; g < nseg; ++g) {
+              const RowMaps& sm_rows = seg_rem[g] ? rows_remote : rows_local;
+              int off = seg_off[g], left = seg_len[g];
+              for (int b = kRowMaps - 1; b >= 0; --b) {
+                const int bh = 8 << b;
+                if (left < bh) continue;
+                const int r0 = int(seg_row[g] + (off - seg_off[g]));
+                tma_load_2d_pair(&sm_rows.m[b], bar, b_dst + off * 128, kc * KB, r0);
+                tma_load_2d_pair(&sm_rows.m[b], bar, b_dst + kBHalf + off * 128, kc * KB + BK, r0);
+                off += bh;
+                left -= bh;
+              }
+            }
+          } else {
+            tma_load_2d_pair(&rm.m[bm], bar, b_dst, kc * KB, int(row_base));
+            tma_load_2d_pair(&rm.m[bm], bar, b_dst + kBHalf, kc * KB + BK, int(row_base));
+          }
           sm.fills[st] += 1;
         }
         if (stop) break;
@@ -803,7 +895,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (;; ++lt) {
         const int t = wait_tile(sm, lt, pipe_bound);
         if (t < 0) break;
-        const Tile tl = decode_tile(s, W, El, me, p.local_first, t);
+        const Tile tl = decode_tile(s, W, El, me, p.local_first, t, p.merged);
         const uint32_t acc = lt & 1, use = lt >> 1;
         const uint64_t ta0 = TRACE_NOW(p);
         if (!mbar_wait(&sm.tempty[acc], (use & 1) ^ 1, pipe_bound, sm, true)) break;
@@ -861,7 +953,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int t = wait_tile(sm, lt, pipe_bound);
       if (p.glu && !named_bar_and(kNamedBarEpi, kEpiWarps * 32, t >= 0)) t = -1;
       if (t < 0) break;
-      const Tile tl = decode_tile(s, W, El, me, p.local_first, t);
+      const Tile tl = decode_tile(s, W, El, me, p.local_first, t, p.merged);
       const uint32_t acc = lt & 1, use = lt >> 1;
       const uint64_t tp0 = TRACE_NOW(p);
       bool full = mbar_wait(&sm.tfull[acc], use & 1, pipe_bound, sm);
@@ -902,9 +994,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int row = tl.row0 + jc * 32 + i;
             const int f = fbase + part * 8;
             if (row < tl.row1 && f + 8 <= p.out_cols) {
-              const uint4 v = *reinterpret_cast<const uint4*>(stage + i * 32 + part * 8);
-              if (p.ret) st_v4(ret_row_ptr(s, p, tl, row) + size_t(f) * 2, v);  // NVLink for remote rows
-              else *reinterpret_cast<uint4*>(p.out + out_row_of(s, p, tl, row) * p.out_cols + f) = v;
+              Tile ts = tl;  // the row's own part (merged tiles hold local and remote rows)
+              int rr = row;
+              bool keep = true;
+              if (tl.merged) {
+                ts.remote = row >= tl.lr8;
+                rr = ts.remote ? row - tl.lr8 : row;
+                keep = ts.remote || row < tl.lr;  // [lr, lr8) is padding
+              }
+              if (keep) {
+                const uint4 v = *reinterpret_cast<const uint4*>(stage + i * 32 + part * 8);
+                if (p.ret) st_v4(ret_row_ptr(s, p, ts, rr) + size_t(f) * 2, v);  // NVLink for remote rows
+                else *reinterpret_cast<uint4*>(p.out + out_row_of(s, p, ts, rr) * p.out_cols + f) = v;
+              }
             }
           }
         }
@@ -1270,7 +1372,7 @@ int launch_fused(const moe_ep_run_params* a, const FusedMode& m, cudaStream_t st
     return kBadArg;
   if (a->num_ctas & 1u) return kBadArg;  // CTA pairs
   if (a->push_ctas < 0 || (a->push_ctas & 1) || a->local_first < 0 || a->local_first > El) return kBadArg;
-  if (a->push_warps < 0 || a->push_warps > kMaxPushWarps || (a->push_mode & ~7) || (a->sched_mode & ~1))
+  if (a->push_warps < 0 || a->push_warps > kMaxPushWarps || (a->push_mode & ~7) || (a->sched_mode & ~3))
     return kBadArg;
   // Rows of the token buffer (the local TMA map's extent).
   const int64_t rows_in = m.general ? m.send_rows : int64_t(W) * El * a->gm;
@@ -1343,8 +1445,9 @@ int launch_fused(const moe_ep_run_params* a, const FusedMode& m, cudaStream_t st
   p.push_bulk = (a->push_mode & MOE_EP_PUSH_BULK) != 0;
   p.push_phased = (a->push_mode & MOE_EP_PUSH_BY_DESTINATION) != 0;
   p.push_hybrid = (a->push_mode & MOE_EP_PUSH_HYBRID) != 0;
-  p.ready_first = (a->sched_mode & MOE_EP_SCHED_READY_FIRST) != 0 && W > 1;
-  p.local_first = p.ready_first ? El : a->local_first;
+  p.merged = (a->sched_mode & MOE_EP_SCHED_MERGED) != 0 && W > 1;
+  p.ready_first = (a->sched_mode & MOE_EP_SCHED_READY_FIRST) != 0 && W > 1 && !p.merged;
+  p.local_first = p.merged ? 0 : p.ready_first ? El : a->local_first;
   p.send_counts = a->counts_are_send != 0;
 
   const size_t smem = fused_smem_bytes();

@@ -86,14 +86,21 @@ def _worker(rank, world, port, cases, q):
             # dispatch placements: CTAs that only push (loads and stores, or
             # bulk copies), more push warps, local tiles first, senders going
             # through destinations one at a time
-            for pc, lf, pw, pm, rf in ((8, El // 2, 2, 0, 0), (2, El, 2, 0, 0), (0, El, 4, 0, 0), (0, 0, 3, 2, 0),
-                                       (8, El, 2, 1, 0), (4, 0, 2, 3, 0), (6, El, 2, 5, 0), (0, 0, 2, 0, 1),
-                                       (0, 0, 4, 2, 1)):
+            for pc, lf, pw, pm, sched in ((8, El // 2, 2, 0, 0), (2, El, 2, 0, 0), (0, El, 4, 0, 0), (0, 0, 3, 2, 0),
+                                          (8, El, 2, 1, 0), (4, 0, 2, 3, 0), (6, El, 2, 5, 0), (0, 0, 2, 0, 1),
+                                          (0, 0, 4, 2, 1), (0, 0, 2, 0, 2), (8, 0, 2, 1, 2)):
                 for k in range(2):
-                    check(f"push_ctas={pc} local_first={lf} push_warps={pw} push_mode={pm} ready_first={rf} call {k}",
+                    check(f"push_ctas={pc} local_first={lf} push_warps={pw} push_mode={pm} sched={sched} call {k}",
                           apg.run(rank, coal, chunk, 1, wl.T, wl.H, wl.E, world, None, False, w.cuda(), rc,
                                   timeout_s=10.0, push_ctas=pc, local_first=lf, push_warps=pw, push_mode=pm,
-                                  ready_first=bool(rf)))
+                                  ready_first=bool(sched & 1), merged=bool(sched & 2)))
+            # merged tiles through the unpadded exchange and the return path's row mapping
+            ref_cm = oracle.compact_from_padded(ref, rcm)
+            coal_m, total_m, _ = utils.dispatch(tok.cuda(), ids.cuda(), wl.E, world, general_a2a=True)
+            om = apg.run(rank, coal_m, total_m, 1, wl.T, wl.H, wl.E, world, None, True, w.cuda(), rc,
+                         timeout_s=10.0, merged=True).float().cpu().numpy()
+            if om.shape != ref_cm.shape or not np.allclose(om, ref_cm, rtol=RTOL, atol=ATOL):
+                errs.append("general + merged: allclose failed")
             # from token rows and ids, counts exchanged inside the kernel
             for k in range(2):
                 check(f"layer call {k}", apg.layer(tok.cuda(), ids.cuda(), wl.E, w.cuda(), timeout_s=10.0,
