@@ -343,9 +343,11 @@ __device__ __forceinline__ Tile decode_tile(const Sched& s, int W, int El, int m
     const int i = r % s.loc_nt[c];
     const int run = s.seg[c * (W + 1) + W];
     tl.lr = s.cnt[me * El + c];
-    tl.lr8 = run > 0 ? (tl.lr + 7) & ~7 : tl.lr;
+    // The local/remote boundary is 8-row aligned even without remote rows:
+    // every CTA half then splits into whole 8-row boxes.
+    tl.lr8 = (tl.lr + 7) & ~7;
     tl.row0 = i * s.loc_tr[c];
-    tl.row1 = min(tl.row0 + s.loc_tr[c], tl.lr8 + run);
+    tl.row1 = min(tl.row0 + s.loc_tr[c], run > 0 ? tl.lr8 + run : tl.lr);
     tl.remote = tl.row1 > tl.lr8;
     tl.n = (tl.row1 - tl.row0 + 15) & ~15;
     return tl;
