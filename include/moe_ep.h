@@ -216,10 +216,11 @@ typedef struct moe_ep_run_params {
  * otherwise (local tiles from their own counter), so that local work fills
  * the waits for rows in flight; local_first is then ignored. */
 #define MOE_EP_SCHED_READY_FIRST 1
-/* MERGED (more than one rank; overrides READY_FIRST and local_first): an
- * expert's local and remote rows are cut into tiles together (local rows,
- * padded to 8, then remote rows), so each weight slice is streamed by as few
- * tiles as the expert's rows need. */
+/* MERGED (more than one rank): an expert whose local rows (padded to 8) and
+ * remote rows together fit 128 rows gets one tile per weight slice covering
+ * both, instead of a local and a remote tile that each stream the slice
+ * (small experts are weight-bound: decode shapes); larger experts keep
+ * separate local and remote tiles. */
 #define MOE_EP_SCHED_MERGED 2
 
 /* push_mode bits.  BULK: push CTAs move rows with TMA bulk copies (local rows

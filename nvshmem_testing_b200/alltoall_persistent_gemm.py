@@ -203,9 +203,8 @@ def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: in
     ``push_warps`` / ``push_mode`` (how rows move, see ``push_setup``),
     ``ready_first`` (more than one rank: remote tiles whose rows have landed
     first, local tiles while none has; ``local_first`` is then ignored),
-    ``merged`` (more than one rank: an expert's local and remote rows cut
-    into tiles together, so each weight slice is streamed by fewer tiles;
-    overrides ``ready_first`` and ``local_first``),
+    ``merged`` (more than one rank: an expert whose local and remote rows
+    together fit 128 rows gets one tile per weight slice instead of two),
     ``send_counts`` (padded path only: this rank's ``[W*El]`` per-expert
     counts, i.e. the routing's ``lengths``, in place of ``recv_counts``; the
     kernel's count exchange then replaces the count all-to-all of

@@ -86,6 +86,7 @@ constexpr int kMaxCells = 512;                  // W * El
 constexpr int kMaxLocalExperts = 256;
 constexpr uint32_t kAccCols = kMaxTileRows;
 constexpr uint32_t kTmemCols = 2 * kAccCols;
+constexpr int kMergeMaxRows = 128;             // merged tiles only for experts this small (local padded + remote)
 constexpr int kGoSlots = 8;                     // > kStages: the leader runs at most kStages k-blocks ahead
 constexpr int kRowMaps = 5;                     // B boxes of 8, 16, 32, 64, 128 rows
 constexpr int kNamedBarPush = 1;
@@ -331,27 +332,10 @@ __device__ __forceinline__ void tile_remote_rows(const Tile& tl, int& lo, int& h
 // that share a weight slice run back to back on neighbouring clusters and
 // read it once from HBM.  With local_first = X > 0 the local tiles of
 // experts [0, X) come first of all (same order among themselves), and those
-// experts' cells then hold only their remote tiles.
+// experts' cells then hold only their remote tiles.  A merged expert (merged
+// mode, small experts with remote rows: no separate remote tiles) counts its
+// merged tiles as its local tiles.
 __device__ __forceinline__ Tile decode_tile(const Sched& s, int W, int El, int me, int lf, int t, bool merged) {
-  if (merged) {  // one row space per expert: local rows, padding to 8, remote rows
-    const int c = find_cell(s.tile_pfx, El, t);
-    const int r = t - s.tile_pfx[c];
-    Tile tl;
-    tl.le = c;
-    tl.merged = 1;
-    tl.feat = r / s.loc_nt[c];
-    const int i = r % s.loc_nt[c];
-    const int run = s.seg[c * (W + 1) + W];
-    tl.lr = s.cnt[me * El + c];
-    // The local/remote boundary is 8-row aligned even without remote rows:
-    // every CTA half then splits into whole 8-row boxes.
-    tl.lr8 = (tl.lr + 7) & ~7;
-    tl.row0 = i * s.loc_tr[c];
-    tl.row1 = min(tl.row0 + s.loc_tr[c], run > 0 ? tl.lr8 + run : tl.lr);
-    tl.remote = tl.row1 > tl.lr8;
-    tl.n = (tl.row1 - tl.row0 + 15) & ~15;
-    return tl;
-  }
   const int lf_total = s.lf_pfx[lf];
   int c, r, lnt, nrt;
   if (t < lf_total) {
@@ -367,13 +351,25 @@ __device__ __forceinline__ Tile decode_tile(const Sched& s, int W, int El, int m
   }
   Tile tl;
   tl.le = c;
-  tl.merged = 0;
-  tl.lr = tl.lr8 = 0;
   tl.feat = r / nrt;
   int i = r % nrt;
+  const int run = s.seg[c * (W + 1) + W];
+  if (merged && s.rem_nt[c] == 0 && run > 0) {
+    // One row space: local rows, padding to an 8-row boundary, remote rows.
+    tl.merged = 1;
+    tl.lr = s.cnt[me * El + c];
+    tl.lr8 = (tl.lr + 7) & ~7;
+    tl.row0 = i * s.loc_tr[c];
+    tl.row1 = min(tl.row0 + s.loc_tr[c], tl.lr8 + run);
+    tl.remote = tl.row1 > tl.lr8;
+    tl.n = (tl.row1 - tl.row0 + 15) & ~15;
+    return tl;
+  }
+  tl.merged = 0;
+  tl.lr = tl.lr8 = 0;
   tl.remote = i >= lnt;
   if (tl.remote) i -= lnt;
-  const int rows = tl.remote ? s.seg[tl.le * (W + 1) + W] : s.cnt[me * El + tl.le];
+  const int rows = tl.remote ? run : s.cnt[me * El + tl.le];
   const int tr = tl.remote ? s.rem_tr[tl.le] : s.loc_tr[tl.le];
   tl.row0 = i * tr;
   tl.row1 = min(tl.row0 + tr, rows);
@@ -495,8 +491,12 @@ __device__ void build_schedule(const Params& p, Sched& s, Smem& sm) {
     }
     sg[W] = run;
     const int lr = s.cnt[me * El + le];
-    if (p.merged) {  // one row space: local rows, padding to 8, remote rows
-      const int v = run > 0 ? ((lr + 7) & ~7) + run : lr;
+    // Merged mode merges small experts only: their tiles are weight-bound, so
+    // one tile instead of a local and a remote one halves their weight
+    // reads; larger experts keep separate tiles (whole boxes, and local rows
+    // that need no NVLink wait).
+    if (p.merged && run > 0 && ((lr + 7) & ~7) + run <= kMergeMaxRows) {
+      const int v = ((lr + 7) & ~7) + run;
       s.loc_tr[le] = tile_rows(v, p.tile_cap);
       s.loc_nt[le] = (v + s.loc_tr[le] - 1) / s.loc_tr[le];
       s.rem_tr[le] = 16;
@@ -1448,8 +1448,8 @@ int launch_fused(const moe_ep_run_params* a, const FusedMode& m, cudaStream_t st
   p.push_phased = (a->push_mode & MOE_EP_PUSH_BY_DESTINATION) != 0;
   p.push_hybrid = (a->push_mode & MOE_EP_PUSH_HYBRID) != 0;
   p.merged = (a->sched_mode & MOE_EP_SCHED_MERGED) != 0 && W > 1;
-  p.ready_first = (a->sched_mode & MOE_EP_SCHED_READY_FIRST) != 0 && W > 1 && !p.merged;
-  p.local_first = p.merged ? 0 : p.ready_first ? El : a->local_first;
+  p.ready_first = (a->sched_mode & MOE_EP_SCHED_READY_FIRST) != 0 && W > 1;
+  p.local_first = p.ready_first ? El : a->local_first;
   p.send_counts = a->counts_are_send != 0;
 
   const size_t smem = fused_smem_bytes();
