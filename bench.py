@@ -349,6 +349,11 @@ class LayerCase:
         and the NVLink bandwidth the dispatch reached."""
         sms = torch.cuda.get_device_properties(self.dev).multi_processor_count
         tr = torch.zeros(sms * _native.TRACE_WORDS, dtype=torch.int64, device=self.dev)
+        # Start every rank together, so no rank's timeline holds another
+        # rank's late start as waiting.
+        torch.cuda.synchronize()
+        if dist.is_initialized():
+            dist.barrier()
         self.step(trace=tr)
         torch.cuda.synchronize()
         t = tr.view(-1, _native.TRACE_WORDS).cpu()

@@ -233,6 +233,10 @@ typedef struct moe_ep_run_params {
 /* HYBRID: with push CTAs, the computing CTAs' push_warps warps move rows too
  * (all take items from one counter). */
 #define MOE_EP_PUSH_HYBRID 4
+/* L2_STREAM: the push's loads of the send buffer and the stores of the
+ * output mark their lines evict-first in L2 (each is touched once), so that
+ * L2 keeps the weight slices and rows that several tiles read. */
+#define MOE_EP_PUSH_L2_STREAM 8
 
 /* Device timeline (globaltimer ns, or counts), one record per CTA. */
 #define MOE_EP_TRACE_WORDS 24

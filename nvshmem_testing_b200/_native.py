@@ -17,7 +17,7 @@ STATUS_NAMES = {OK: "ok", BAD_ARG: "bad argument", CUDA_ERR: "CUDA error", TIMEO
                 CAPACITY: "receive capacity exceeded", BAD_ROUTE: "bad routing input",
                 SCRATCH_LIMIT: "size exceeds the fixed scratch of moe_ep_run_noalloc"}
 NOALLOC_MAX_EXPERTS = 64
-PUSH_BULK, PUSH_BY_DESTINATION, PUSH_HYBRID = 1, 2, 4
+PUSH_BULK, PUSH_BY_DESTINATION, PUSH_HYBRID, PUSH_L2_STREAM = 1, 2, 4, 8
 SCHED_READY_FIRST, SCHED_MERGED = 1, 2
 ABI_VERSION = 3
 

@@ -74,11 +74,11 @@ def push_setup(push_warps: int | None = None, push_mode: int | None = None) -> t
     """(push_warps, push_mode): warps per CTA that move rows when no push
     CTAs are used, and the MOE_EP_PUSH_* bits (1: bulk copies in push CTAs,
     2: destination-major order, 4: computing CTAs push beside the push
-    CTAs)."""
+    CTAs, 8: send-buffer loads and output stores evict-first in L2)."""
     pw = DEFAULT_PUSH_WARPS if push_warps is None else int(push_warps)
     pm = DEFAULT_PUSH_MODE if push_mode is None else int(push_mode)
-    if not 1 <= pw <= 6 or pm & ~7:
-        raise ValueError(f"push_warps must be 1..6 and push_mode a combination of the MOE_EP_PUSH_* bits 1, 2, 4, "
+    if not 1 <= pw <= 6 or pm & ~15:
+        raise ValueError(f"push_warps must be 1..6 and push_mode a combination of the MOE_EP_PUSH_* bits 1, 2, 4, 8, "
                          f"got {pw}, {pm}")
     return pw, pm
 

@@ -138,6 +138,9 @@ struct Params {
   // With push CTAs, the computing CTAs' push_warps warps push as well
   // (both take items from the same counter).
   int push_hybrid;
+  // Send-buffer loads of the push and the output's stores marked evict-first
+  // in L2 (each byte is touched once), keeping L2 for weights and rows.
+  int l2_stream;
   // Tile order: the local tiles of experts [0, local_first) come before any
   // remote tile, so the GEMM starts on rows that need no NVLink transfer.
   int local_first;
@@ -602,17 +605,25 @@ __device__ void zero_fill(const Params& p, const Sched& s, int z, int pt, int np
 
 // One push item's rows: nvec 16-byte vectors from this GPU's send buffer to
 // a peer's receive region, U loads in flight per thread before their stores.
+// With `stream`, the loads of the send buffer (read once) are marked
+// evict-first in L2, so they do not push the GEMM's weights and rows out.
 template <int U>
-__device__ __forceinline__ void copy_rows(const uint4* src, uint4* dst, int64_t nvec, int pt, int np) {
+__device__ __forceinline__ void copy_rows(const uint4* src, uint4* dst, int64_t nvec, int pt, int np, bool stream) {
+  const uint64_t pol = l2_policy_evict_first();
   int64_t v = pt;
   for (; v + (U - 1) * np < nvec; v += U * np) {
     uint4 a[U];
+    if (stream) {
 #pragma unroll
-    for (int u = 0; u < U; ++u) a[u] = ld_nc_v4(src + v + u * np);
+      for (int u = 0; u < U; ++u) a[u] = ld_nc_v4_hint(src + v + u * np, pol);
+    } else {
+#pragma unroll
+      for (int u = 0; u < U; ++u) a[u] = ld_nc_v4(src + v + u * np);
+    }
 #pragma unroll
     for (int u = 0; u < U; ++u) st_v4(dst + v + u * np, a[u]);
   }
-  for (; v < nvec; v += np) st_v4(dst + v, ld_nc_v4(src + v));
+  for (; v < nvec; v += np) st_v4(dst + v, stream ? ld_nc_v4_hint(src + v, pol) : ld_nc_v4(src + v));
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -945,6 +956,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tempty_leader = mapa_shared(smem_u32(&sm.tempty[0]), 0);
     uint32_t lt = 0;
     uint64_t epi_ns = 0;
+    const uint64_t out_pol = l2_policy_evict_first();
     // SwiGLU mode: quarters 0 and 1 hold gate features, 2 and 3 the matching
     // up features; a gate warp reads its partner's staged values.  The four
     // warps meet at named barriers, so they decide together whether to go on
@@ -1007,6 +1019,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (keep) {
                 const uint4 v = *reinterpret_cast<const uint4*>(stage + i * 32 + part * 8);
                 if (p.ret) st_v4(ret_row_ptr(s, p, ts, rr) + size_t(f) * 2, v);  // NVLink for remote rows
+                else if (p.l2_stream) st_v4_hint(p.out + out_row_of(s, p, ts, rr) * p.out_cols + f, v, out_pol);
                 else *reinterpret_cast<uint4*>(p.out + out_row_of(s, p, ts, rr) * p.out_cols + f) = v;
               }
             }
@@ -1063,8 +1076,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                                               (size_t(par) * p.cap_rows + s.push_off[d * El + le] + j0) * row_bytes);
         const int64_t nvec = int64_t(j1 - j0) * int64_t(row_bytes / 16);
         // More loads in flight per thread where a whole CTA pushes.
-        if (push_cta) copy_rows<16>(src, dst, nvec, pt, np);
-        else copy_rows<4>(src, dst, nvec, pt, np);
+        if (push_cta) copy_rows<16>(src, dst, nvec, pt, np, p.l2_stream);
+        else copy_rows<4>(src, dst, nvec, pt, np, p.l2_stream);
         fence_acq_rel_sys();
         named_bar_sync(kNamedBarPush, np);
         if (pt == 0) {
@@ -1374,7 +1387,7 @@ int launch_fused(const moe_ep_run_params* a, const FusedMode& m, cudaStream_t st
     return kBadArg;
   if (a->num_ctas & 1u) return kBadArg;  // CTA pairs
   if (a->push_ctas < 0 || (a->push_ctas & 1) || a->local_first < 0 || a->local_first > El) return kBadArg;
-  if (a->push_warps < 0 || a->push_warps > kMaxPushWarps || (a->push_mode & ~7) || (a->sched_mode & ~3))
+  if (a->push_warps < 0 || a->push_warps > kMaxPushWarps || (a->push_mode & ~15) || (a->sched_mode & ~3))
     return kBadArg;
   // Rows of the token buffer (the local TMA map's extent).
   const int64_t rows_in = m.general ? m.send_rows : int64_t(W) * El * a->gm;
@@ -1447,6 +1460,7 @@ int launch_fused(const moe_ep_run_params* a, const FusedMode& m, cudaStream_t st
   p.push_bulk = (a->push_mode & MOE_EP_PUSH_BULK) != 0;
   p.push_phased = (a->push_mode & MOE_EP_PUSH_BY_DESTINATION) != 0;
   p.push_hybrid = (a->push_mode & MOE_EP_PUSH_HYBRID) != 0;
+  p.l2_stream = (a->push_mode & MOE_EP_PUSH_L2_STREAM) != 0;
   p.merged = (a->sched_mode & MOE_EP_SCHED_MERGED) != 0 && W > 1;
   p.ready_first = (a->sched_mode & MOE_EP_SCHED_READY_FIRST) != 0 && W > 1;
   p.local_first = p.ready_first ? El : a->local_first;

@@ -339,6 +339,28 @@ __device__ __forceinline__ void bulk_wait() {
   asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// An L2 access policy that marks the lines an access touches as the first to
+// evict (data read or written once: the send buffer, the layer's output).
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+// 16-byte load, not allocated in L1, with an L2 access policy.
+__device__ __forceinline__ uint4 ld_nc_v4_hint(const void* p, uint64_t pol) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p), "l"(pol));
+  return v;
+}
+// 16-byte store with an L2 access policy.
+__device__ __forceinline__ void st_v4_hint(void* p, uint4 v, uint64_t pol) {
+  asm volatile("st.global.L2::cache_hint.v4.u32 [%0], {%1,%2,%3,%4}, %5;" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w), "l"(pol)
+               : "memory");
+}
+
 // 16-byte streaming load that does not allocate in L1.
 __device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
   uint4 v;

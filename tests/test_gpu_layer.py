@@ -83,6 +83,18 @@ def test_run_repeated_calls_are_stable(single_rank_group):
     assert torch.equal(first, again)
 
 
+def test_l2_stream_hints_give_the_same_output(single_rank_group):
+    """push_mode=8 (evict-first L2 hints on the output's stores) changes
+    no bit of the output."""
+    El, H, N, gm, counts = 5, 256, 520, 300, [1, 299, 128, 129, 0]
+    tok, w = _make(El, H, N, gm, counts, seed=21)
+    rc = torch.tensor([counts], dtype=torch.int32).cuda()
+    plain = apg.run(0, tok.cuda(), El * gm, 1, El * gm, H, El, 1, None, False, w.cuda(), rc, check=True)
+    hinted = apg.run(0, tok.cuda(), El * gm, 1, El * gm, H, El, 1, None, False, w.cuda(), rc, check=True,
+                     push_mode=8)
+    assert torch.equal(plain, hinted)
+
+
 def test_baseline_entry_point_treats_all_rows_valid(single_rank_group):
     El, H, N, gm = 2, 128, 128, 64
     tok, w = _make(El, H, N, gm, [64, 64], seed=11)

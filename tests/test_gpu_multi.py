@@ -85,10 +85,11 @@ def _worker(rank, world, port, cases, q):
                 check(f"call {k}", o_)
             # dispatch placements: CTAs that only push (loads and stores, or
             # bulk copies), more push warps, local tiles first, senders going
-            # through destinations one at a time
+            # through destinations one at a time, evict-first L2 hints
             for pc, lf, pw, pm, sched in ((8, El // 2, 2, 0, 0), (2, El, 2, 0, 0), (0, El, 4, 0, 0), (0, 0, 3, 2, 0),
                                           (8, El, 2, 1, 0), (4, 0, 2, 3, 0), (6, El, 2, 5, 0), (0, 0, 2, 0, 1),
-                                          (0, 0, 4, 2, 1), (0, 0, 2, 0, 2), (8, 0, 2, 1, 2)):
+                                          (0, 0, 4, 2, 1), (0, 0, 2, 0, 2), (8, 0, 2, 1, 2), (0, El, 2, 8, 0),
+                                          (8, 0, 2, 9, 2)):
                 for k in range(2):
                     check(f"push_ctas={pc} local_first={lf} push_warps={pw} push_mode={pm} sched={sched} call {k}",
                           apg.run(rank, coal, chunk, 1, wl.T, wl.H, wl.E, world, None, False, w.cuda(), rc,
