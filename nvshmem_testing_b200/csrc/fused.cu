@@ -430,14 +430,20 @@ __device__ void warp_exclusive_scan(int* a, int n, int lane) {
 // Build the schedule for this call from the full count matrix.  All ranks
 // hold identical matrices, so every validation failure is seen by all ranks.
 // Every step is parallel over (rank, expert) cells; prefix sums are warp
-// scans over shared memory.
-__device__ void build_schedule(const Params& p, Sched& s, Smem& sm) {
+// scans over shared memory.  The matrix is first copied in one coalesced
+// pass into `scratch` (the stage memory, unused until the schedule exists),
+// so the per-cell loops below read shared memory, not dependent L2 loads.
+__device__ void build_schedule(const Params& p, Sched& s, Smem& sm, int32_t* scratch) {
   const int W = p.W, El = p.El, me = p.me, tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const uint32_t par = p.epoch & 1u;
   // One rank reads its own recv_counts (nothing was exchanged).
-  const int32_t* cm = W == 1 ? p.recv_counts
-                             : reinterpret_cast<const int32_t*>(p.local + p.off_cmat) + size_t(par) * W * W * El;
+  const int32_t* cm_g = W == 1 ? p.recv_counts
+                               : reinterpret_cast<const int32_t*>(p.local + p.off_cmat) + size_t(par) * W * W * El;
+  const int ncm = W * W * El;
+  for (int i = tid; i < ncm; i += kThreads) scratch[i] = cm_g[i];
+  __syncthreads();
+  const int32_t* cm = scratch;
   // C(owner, src, le): rows src sends to owner's local expert le.  The
   // matrix holds every rank's published block: receive counts (block =
   // owner) or send counts (block = src).
@@ -720,8 +726,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     TRACE_SET(p, MOE_EP_TRACE_COUNTS, TRACE_NOW(p));
   }
   __syncthreads();
-  if (!aborted(sm)) build_schedule(p, s, sm);
+  if (!aborted(sm)) build_schedule(p, s, sm, reinterpret_cast<int32_t*>(stage_mem));
   __syncthreads();
+  // The stage memory held the count matrix (generic proxy); TMA writes it next.
+  fence_proxy_async_smem();
   const bool run_main = !aborted(sm);
   if (tid == 0) TRACE_SET(p, MOE_EP_TRACE_SCHED, TRACE_NOW(p));
 
@@ -1240,30 +1248,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     tmem_dealloc_pair(tmem_base, kTmemCols);
   }
-  if (tid == 0) {
-    if (p.ret) __threadfence_system();
-    else __threadfence();
-    const uint32_t old = atomicAdd(&lw->done_ctr[par], 1u);
-    if (old == gridDim.x - 1) {
+  if (warp == 0) {
+    uint32_t old = 0;
+    if (lane == 0) {
       if (p.ret) __threadfence_system();
       else __threadfence();
-      lw->push_ctr[par ^ 1] = 0;
-      lw->zero_ctr[par ^ 1] = 0;
-      lw->local_ctr[par ^ 1] = 0;
-      lw->tile_ctr[par ^ 1] = 0;
-      lw->done_ctr[par ^ 1] = 0;
-      __threadfence();
-      for (int q = 0; q < W; ++q) {
+      old = atomicAdd(&lw->done_ctr[par], 1u);
+      if (old == gridDim.x - 1) {
+        if (p.ret) __threadfence_system();
+        else __threadfence();
+        lw->push_ctr[par ^ 1] = 0;
+        lw->zero_ctr[par ^ 1] = 0;
+        lw->local_ctr[par ^ 1] = 0;
+        lw->tile_ctr[par ^ 1] = 0;
+        lw->done_ctr[par ^ 1] = 0;
+        __threadfence();
+      }
+    }
+    old = __shfl_sync(0xffffffffu, old, 0);
+    __syncwarp();
+    if (old == gridDim.x - 1) {
+      // The last CTA: lane q releases "free" (and, with return rows, "rows
+      // returned") to rank q, so the W system-scope releases run side by
+      // side instead of one NVLink round trip after another.  After an error
+      // the return flags stay unset and the sources' combine waits time out.
+      const bool returned = p.ret && ld_volatile_u32(&lw->status) == 0;
+      for (int q = lane; q < W; q += 32) {
         unsigned char* peer = reinterpret_cast<unsigned char*>(p.peers[q]);
         st_release_sys(at_u32(peer, p.off_free) + me, p.epoch);
-      }
-      // Every CTA's return rows are out: tell each source rank.  After an
-      // error nothing is released and the sources' combine waits time out.
-      if (p.ret && ld_volatile_u32(&lw->status) == 0) {
-        for (int q = 0; q < W; ++q) {
-          unsigned char* peer = reinterpret_cast<unsigned char*>(p.peers[q]);
-          st_release_sys(at_u32(peer, p.off_rflag) + me, p.epoch);
-        }
+        if (returned) st_release_sys(at_u32(peer, p.off_rflag) + me, p.epoch);
       }
     }
   }
@@ -1353,6 +1366,9 @@ struct DeviceLaunchInfo {
 };
 static DeviceLaunchInfo g_launch_info[kMaxDevices];
 
+// The count matrix (W <= 64 ranks, W * El <= kMaxCells) fits the stage
+// memory that build_schedule copies it into.
+static_assert(size_t(64) * kMaxCells * 4 <= size_t(kStages) * kStageBytes, "count matrix exceeds the stage memory");
 static_assert(sizeof(Sched) % 16 == 0 && kEpiStageBytes % 16 == 0 && (kStages * kStageBytes) % 1024 == 0,
               "Sched and Smem must start on 16-byte boundaries");
 // The whole shared-memory plan must fit the 227 KB a CTA may opt in to.
