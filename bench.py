@@ -223,6 +223,12 @@ def nccl_layer_combine(tokens, chunk, world, weights, ids, vals, slots):
     return (back[rows].float() * w[..., None]).sum(dim=1).to(torch.bfloat16)
 
 
+# Host time per call of the last ``time_device`` loop (ms): how long the
+# host took to issue one step.  A step whose device time is close to this
+# is bound by the host's launch path, not by the GPU.
+LAST_HOST_MS = [0.0]
+
+
 def time_device(fn, steps: int, warmup: int, sampler_device=None):
     sampler = ClockSampler(sampler_device) if sampler_device is not None else None
     for _ in range(warmup):
@@ -233,8 +239,10 @@ def time_device(fn, steps: int, warmup: int, sampler_device=None):
     if sampler:
         sampler.mark_start()
     s.record()
+    h0 = time.perf_counter()
     for _ in range(steps):
         fn()
+    LAST_HOST_MS[0] = (time.perf_counter() - h0) * 1e3 / steps
     e.record()
     torch.cuda.synchronize()
     if sampler:
@@ -451,10 +459,12 @@ def measure_case(case: LayerCase, steps: int, warmup: int, peaks, peaks_src, ncc
     on the same inputs and the roofline."""
     ok = case.allclose_vs_nccl() if not no_nccl else None
     ms, clocks = time_device(case.step, steps, warmup, sampler_device=sampler_device)
+    host_max = max_over_ranks(LAST_HOST_MS[0])
     ms_max = max_over_ranks(ms)
     flops_total = sum_over_ranks(case.flops_rank)
     r = {"workload": case.name, "us_per_layer": ms_max * 1e3, "value": flops_total / (ms_max * 1e-3) / 1e12,
          "unit": "TFLOP/s", "gm": case.gm, "local_experts": case.El, "parity_vs_nccl_allclose": ok,
+         "host_us_per_call": host_max * 1e3,
          "roofline": case.roofline(ms_max, peaks, peaks_src), "_flops_total": flops_total, "_ms": ms_max,
          "_clocks": clocks}
     if not no_nccl:
