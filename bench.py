@@ -1143,6 +1143,7 @@ def main(argv=None) -> int:
                    "ready_first": apg.DEFAULT_READY_FIRST and world > 1, "merged": apg.DEFAULT_MERGED and world > 1,
                    "push_rows": apg.DEFAULT_PUSH_ROWS},
         "parity_vs_nccl_allclose": head["parity_vs_nccl_allclose"],
+        "host_us_per_call": head["host_us_per_call"],
         "parity_oracle": parity,
         "roofline": head["roofline"],
         "cpu_baseline": None,

@@ -222,6 +222,17 @@ typedef struct moe_ep_run_params {
  * (small experts are weight-bound: decode shapes); larger experts keep
  * separate local and remote tiles. */
 #define MOE_EP_SCHED_MERGED 2
+/* Bits 4-7: row groups G for the remote tiles of each expert (more than one
+ * rank).  Feature-major order (every row tile of a weight slice, then the
+ * next slice) needs all of an expert's remote rows within the first slices;
+ * with G > 1 the expert's remote row tiles are split into G contiguous
+ * groups, taken one after another, each feature-major, so the tiles of rows
+ * that land first (sources arrive in order me+1, me+2, ...) run first, at
+ * the cost of reading each weight slice from HBM once per group.  0 chooses:
+ * W-1 groups for an expert whose remote tiles per group would still fill
+ * every computing pair (large experts: Mixtral's shapes), else 1. */
+#define MOE_EP_SCHED_ROW_GROUPS_SHIFT 4
+#define MOE_EP_SCHED_ROW_GROUPS_MASK 0xF0
 
 /* push_mode bits.  BULK: push CTAs move rows with TMA bulk copies (local rows
  * through a ring of shared-memory pieces to the peer) instead of loads and

@@ -18,7 +18,7 @@ STATUS_NAMES = {OK: "ok", BAD_ARG: "bad argument", CUDA_ERR: "CUDA error", TIMEO
                 SCRATCH_LIMIT: "size exceeds the fixed scratch of moe_ep_run_noalloc"}
 NOALLOC_MAX_EXPERTS = 64
 PUSH_BULK, PUSH_BY_DESTINATION, PUSH_HYBRID, PUSH_L2_STREAM = 1, 2, 4, 8
-SCHED_READY_FIRST, SCHED_MERGED = 1, 2
+SCHED_READY_FIRST, SCHED_MERGED, SCHED_ROW_GROUPS_SHIFT = 1, 2, 4
 ABI_VERSION = 3
 
 # Every symbol include/moe_ep.h declares.

@@ -53,6 +53,9 @@ DEFAULT_PUSH_MODE = int(os.environ.get("MOE_EP_PUSH_MODE", "0"))
 DEFAULT_READY_FIRST = os.environ.get("MOE_EP_READY_FIRST", "0") not in ("", "0")
 # Merged tiles for small experts (decode shapes) unless switched off.
 DEFAULT_MERGED = os.environ.get("MOE_EP_MERGED", "1") not in ("", "0")
+# Remote row groups per expert (MOE_EP_SCHED_ROW_GROUPS bits): 0 lets the
+# kernel choose (W-1 groups for large experts, else 1).
+DEFAULT_ROW_GROUPS = int(os.environ.get("MOE_EP_ROW_GROUPS", "0"))
 
 
 def placement(W: int, El: int, push_ctas: int | None = None, local_first: int | None = None) -> tuple[int, int]:
@@ -101,7 +104,8 @@ def _launch_params(me: int, W: int, tokens: torch.Tensor, gm: int | None, transm
                    local_weights: torch.Tensor, recv_counts, group, timeout_s, push_rows, num_ctas, trace,
                    ret_cols: int = 0, push_ctas: int | None = None, local_first: int | None = None,
                    send_counts: torch.Tensor | None = None, push_warps: int | None = None,
-                   push_mode: int | None = None, ready_first: bool | None = None, merged: bool | None = None):
+                   push_mode: int | None = None, ready_first: bool | None = None, merged: bool | None = None,
+                   row_groups: int | None = None):
     """Validate the fused layer's inputs and fill ``moe_ep_run_params``.
 
     ``gm`` is the bound on every (rank, expert) count; ``None`` means the
@@ -154,7 +158,11 @@ def _launch_params(me: int, W: int, tokens: torch.Tensor, gm: int | None, transm
     p.push_warps, p.push_mode = push_setup(push_warps, push_mode)
     rf = DEFAULT_READY_FIRST if ready_first is None else bool(ready_first)
     mg = DEFAULT_MERGED if merged is None else bool(merged)
-    p.sched_mode = (N.SCHED_READY_FIRST if (rf and W > 1) else 0) | (N.SCHED_MERGED if (mg and W > 1) else 0)
+    rg = DEFAULT_ROW_GROUPS if row_groups is None else int(row_groups)
+    if not 0 <= rg <= 15:
+        raise ValueError(f"row_groups must be 0..15 (0: chosen by the kernel), got {rg}")
+    p.sched_mode = ((N.SCHED_READY_FIRST if (rf and W > 1) else 0) | (N.SCHED_MERGED if (mg and W > 1) else 0) |
+                    (rg << N.SCHED_ROW_GROUPS_SHIFT))
     p.counts_are_send = int(send_counts is not None)
     p.timeout_ns = int((timeout_s if timeout_s is not None else DEFAULT_TIMEOUT_S) * 1e9)
     p.status_host = ws.status_host.data_ptr()
@@ -185,7 +193,8 @@ def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: in
         check: bool = False, trace: torch.Tensor | None = None, max_count: int | None = None,
         recv_rows: int | None = None, push_ctas: int | None = None, local_first: int | None = None,
         send_counts: torch.Tensor | None = None, push_warps: int | None = None,
-        push_mode: int | None = None, ready_first: bool | None = None, merged: bool | None = None) -> torch.Tensor:
+        push_mode: int | None = None, ready_first: bool | None = None, merged: bool | None = None,
+        row_groups: int | None = None) -> torch.Tensor:
     """Fused dispatch + grouped GEMM; see the module docstring.
 
     ``general_a2a=True`` (a stub in the reference, alltoall_persistent_gemm.py:221-222)
@@ -212,6 +221,9 @@ def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: in
     first, local tiles while none has; ``local_first`` is then ignored),
     ``merged`` (more than one rank: an expert whose local and remote rows
     together fit 128 rows gets one tile per weight slice instead of two),
+    ``row_groups`` (more than one rank: an expert's remote row tiles taken in
+    that many contiguous groups, each feature-major, so rows that land first
+    are computed first; 0 lets the kernel choose, 1 is plain feature-major),
     ``send_counts`` (padded path only: this rank's ``[W*El]`` per-expert
     counts, i.e. the routing's ``lengths``, in place of ``recv_counts``; the
     kernel's count exchange then replaces the count all-to-all of
@@ -240,7 +252,8 @@ def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: in
                                                      recv_counts, group, timeout_s, push_rows, num_ctas, trace,
                                                      push_ctas=push_ctas, local_first=local_first,
                                                      push_warps=push_warps, push_mode=push_mode,
-                                                     ready_first=ready_first, merged=merged)
+                                                     ready_first=ready_first, merged=merged,
+                                                     row_groups=row_groups)
         # A zero-row view has a null data_ptr; the kernel wants a real buffer.
         buf = torch.empty((max(out_rows, 1), Nout), dtype=torch.bfloat16, device=tokens.device)
         out = buf[:out_rows]
@@ -255,7 +268,7 @@ def run(rank: int, tokens: torch.Tensor, transmit_size: int, batch: int, seq: in
                                                      push_ctas=push_ctas, local_first=local_first,
                                                      send_counts=send_counts, push_warps=push_warps,
                                                      push_mode=push_mode, ready_first=ready_first,
-                                                     merged=merged)
+                                                     merged=merged, row_groups=row_groups)
         out = torch.empty((El, W * gm, Nout), dtype=torch.bfloat16, device=tokens.device)
         p.out = out.data_ptr()
         stream = torch.cuda.current_stream(tokens.device)

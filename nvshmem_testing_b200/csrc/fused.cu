@@ -154,6 +154,8 @@ struct Params {
   // need (one, where local + remote rows fit 256) instead of separate local
   // and remote tiles.  local_first and ready_first are then off.
   int merged;
+  // Remote row groups per expert (0: chosen per expert, see decode_tile).
+  int row_groups;
   // recv_counts holds this rank's send counts [W dst][El] instead of its
   // receive counts [W src][El]; every rank publishes its block either way,
   // so the exchanged matrix is read transposed and no host-side count
@@ -178,7 +180,8 @@ struct RowMaps {
 // aligned (Smem holds the 8-byte mbarriers) whatever their arrays add up to.
 struct alignas(16) Sched {
   int nfeat, kblocks;
-  int tiles_total, push_total, zero_total;
+  int row_groups, npairs;  // Params::row_groups; computing CTA pairs
+  int tiles_total, push_total, zero_total, pad_;
   int cnt[kMaxCells];                     // [src][le] rows this rank receives
   int seg[kMaxCells + kMaxLocalExperts];  // [le][q], q = 0..W: compact start of position q (seg[.][1] = 0)
   int rbase[kMaxLocalExperts + 1];        // compact base row of expert le in this rank's receive buffer
@@ -338,10 +341,24 @@ __device__ __forceinline__ void tile_remote_rows(const Tile& tl, int& lo, int& h
 // experts' cells then hold only their remote tiles.  A merged expert (merged
 // mode, small experts with remote rows: no separate remote tiles) counts its
 // merged tiles as its local tiles.
+//
+// Row groups: with G > 1 groups for an expert, its cell holds first its
+// local tiles (feature-major) and then its remote row tiles cut into G
+// contiguous groups, each group feature-major, so the tiles whose rows land
+// first (sources arrive in segment order) do not wait behind tiles of rows
+// still in flight.  G = row_groups if set, else W-1 for an expert whose
+// remote tiles per group still cover every computing pair, else 1.
+__device__ __forceinline__ int remote_groups(const Sched& s, int W, int rem_nt) {
+  int g = s.row_groups;
+  if (g == 0) g = (W > 1 && s.nfeat * rem_nt >= (W - 1) * s.npairs) ? W - 1 : 1;
+  return max(1, min(g, rem_nt));
+}
+
 __device__ __forceinline__ Tile decode_tile(const Sched& s, int W, int El, int me, int lf, int t, bool merged) {
   const int lf_total = s.lf_pfx[lf];
+  const bool in_lf = t < lf_total;
   int c, r, lnt, nrt;
-  if (t < lf_total) {
+  if (in_lf) {
     c = find_cell(s.lf_pfx, lf, t);
     r = t - s.lf_pfx[c];
     lnt = nrt = s.loc_nt[c];
@@ -370,8 +387,33 @@ __device__ __forceinline__ Tile decode_tile(const Sched& s, int W, int El, int m
   }
   tl.merged = 0;
   tl.lr = tl.lr8 = 0;
-  tl.remote = i >= lnt;
-  if (tl.remote) i -= lnt;
+  const int rn = s.rem_nt[c];
+  const int g = in_lf ? 1 : remote_groups(s, W, rn);
+  if (g > 1) {
+    // Local tiles feature-major, then the remote row groups (see above).
+    const int nf = s.nfeat;
+    if (r < nf * lnt) {
+      tl.feat = r / lnt;
+      i = r % lnt;
+      tl.remote = 0;
+    } else {
+      int r2 = r - nf * lnt, start = 0, gi = 0;
+      const int base = rn / g, extra = rn % g;
+      int gs = base + (extra > 0);
+      while (r2 >= nf * gs) {
+        r2 -= nf * gs;
+        start += gs;
+        ++gi;
+        gs = base + (gi < extra);
+      }
+      tl.feat = r2 / gs;
+      i = start + r2 % gs;
+      tl.remote = 1;
+    }
+  } else {
+    tl.remote = i >= lnt;
+    if (tl.remote) i -= lnt;
+  }
   const int rows = tl.remote ? run : s.cnt[me * El + tl.le];
   const int tr = tl.remote ? s.rem_tr[tl.le] : s.loc_tr[tl.le];
   tl.row0 = i * tr;
@@ -456,6 +498,8 @@ __device__ void build_schedule(const Params& p, Sched& s, Smem& sm, int32_t* scr
   if (tid == 0) {
     s.nfeat = nfeat;
     s.kblocks = (p.H + KB - 1) / KB;
+    s.row_groups = p.row_groups;
+    s.npairs = max(1, (int(gridDim.x) - p.push_ctas) / 2);
     s.zero_total = (p.ret || p.general) ? 0 : W * El;  // no padded output in return or compact mode
   }
   // Validation: 0 <= count <= gm everywhere, chunk slots suffice.
@@ -1403,7 +1447,7 @@ int launch_fused(const moe_ep_run_params* a, const FusedMode& m, cudaStream_t st
     return kBadArg;
   if (a->num_ctas & 1u) return kBadArg;  // CTA pairs
   if (a->push_ctas < 0 || (a->push_ctas & 1) || a->local_first < 0 || a->local_first > El) return kBadArg;
-  if (a->push_warps < 0 || a->push_warps > kMaxPushWarps || (a->push_mode & ~15) || (a->sched_mode & ~3))
+  if (a->push_warps < 0 || a->push_warps > kMaxPushWarps || (a->push_mode & ~15) || (a->sched_mode & ~(3 | MOE_EP_SCHED_ROW_GROUPS_MASK)))
     return kBadArg;
   // Rows of the token buffer (the local TMA map's extent).
   const int64_t rows_in = m.general ? m.send_rows : int64_t(W) * El * a->gm;
@@ -1481,6 +1525,7 @@ int launch_fused(const moe_ep_run_params* a, const FusedMode& m, cudaStream_t st
   p.ready_first = (a->sched_mode & MOE_EP_SCHED_READY_FIRST) != 0 && W > 1;
   p.local_first = p.ready_first ? El : a->local_first;
   p.send_counts = a->counts_are_send != 0;
+  p.row_groups = (a->sched_mode & MOE_EP_SCHED_ROW_GROUPS_MASK) >> MOE_EP_SCHED_ROW_GROUPS_SHIFT;
 
   const size_t smem = fused_smem_bytes();
   int dev = 0;

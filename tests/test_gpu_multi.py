@@ -85,16 +85,18 @@ def _worker(rank, world, port, cases, q):
                 check(f"call {k}", o_)
             # dispatch placements: CTAs that only push (loads and stores, or
             # bulk copies), more push warps, local tiles first, senders going
-            # through destinations one at a time, evict-first L2 hints
+            # through destinations one at a time, evict-first L2 hints, remote
+            # row tiles in groups (sched bits 4-7)
             for pc, lf, pw, pm, sched in ((8, El // 2, 2, 0, 0), (2, El, 2, 0, 0), (0, El, 4, 0, 0), (0, 0, 3, 2, 0),
                                           (8, El, 2, 1, 0), (4, 0, 2, 3, 0), (6, El, 2, 5, 0), (0, 0, 2, 0, 1),
                                           (0, 0, 4, 2, 1), (0, 0, 2, 0, 2), (8, 0, 2, 1, 2), (0, El, 2, 8, 0),
-                                          (8, 0, 2, 9, 2)):
+                                          (8, 0, 2, 9, 2), (0, El, 2, 0, 0x20), (0, 0, 2, 0, 0x32),
+                                          (8, 0, 2, 1, 0x31)):
                 for k in range(2):
                     check(f"push_ctas={pc} local_first={lf} push_warps={pw} push_mode={pm} sched={sched} call {k}",
                           apg.run(rank, coal, chunk, 1, wl.T, wl.H, wl.E, world, None, False, w.cuda(), rc,
                                   timeout_s=10.0, push_ctas=pc, local_first=lf, push_warps=pw, push_mode=pm,
-                                  ready_first=bool(sched & 1), merged=bool(sched & 2)))
+                                  ready_first=bool(sched & 1), merged=bool(sched & 2), row_groups=sched >> 4))
             # merged tiles through the unpadded exchange and the return path's row mapping
             ref_cm = oracle.compact_from_padded(ref, rcm)
             coal_m, total_m, _ = utils.dispatch(tok.cuda(), ids.cuda(), wl.E, world, general_a2a=True)
@@ -151,6 +153,8 @@ CASES = [
     ("deepseek_v3", {"T": 512, "H": 256, "N": 384, "E": 16}),
     ("skewed_zipf", {"T": 1024, "H": 128, "N": 136, "E": 8}),
     ("mixtral", {"T": 256, "H": 512, "N": 256}),
+    # two remote row tiles per expert and two weight slices: row groups reorder them
+    ("mixtral", {"T": 2048, "H": 256, "N": 512}),
     ("decode", {"T": 16, "H": 256, "N": 256}),
 ]
 
@@ -166,7 +170,8 @@ def test_all_visible_ranks_match_oracle():
         pytest.skip("needs 3+ GPUs")
     n = 8 if n >= 8 else (4 if n >= 4 else 2)
     _spawn(n, [("deepseek_v3", {"T": 256, "H": 256, "N": 256, "E": 32}),
-               ("skewed_zipf", {"T": 512, "H": 128, "N": 128, "E": 16})])
+               ("skewed_zipf", {"T": 512, "H": 128, "N": 128, "E": 16}),
+               ("mixtral", {"T": 1024, "H": 256, "N": 512})])
 
 
 def test_missing_peer_times_out_with_status(single_rank_group):
