@@ -91,6 +91,7 @@ constexpr int kGoSlots = 8;                     // > kStages: the leader runs at
 constexpr int kRowMaps = 5;                     // B boxes of 8, 16, 32, 64, 128 rows
 constexpr int kNamedBarPush = 1;
 constexpr int kNamedBarEpi = 2;                 // the epilogue warps (SwiGLU mode)
+constexpr int kNamedBarZero = 3;                // zero warps working beside the push warps
 constexpr uint32_t kEpiStageBytes = kEpiWarps * 32 * 32 * 2;  // 32 rows x 32 features bf16 per warp
 
 struct Params {
@@ -676,6 +677,21 @@ __device__ __forceinline__ void copy_rows(const uint4* src, uint4* dst, int64_t 
   for (; v < nvec; v += np) st_v4(dst + v, stream ? ld_nc_v4_hint(src + v, pol) : ld_nc_v4(src + v));
 }
 
+// Zero-fill items (padded output cells) from the shared zero counter until
+// none is left: np threads of one group (pt = this thread), `slot` the
+// group's shared-memory word for the claimed item, `bar` its named barrier.
+__device__ void zero_items(const Params& p, const Sched& s, Smem& sm, LocalWords* lw, uint32_t par, int* slot,
+                           int bar, int np, int pt) {
+  for (;;) {
+    if (pt == 0) *slot = aborted(sm) ? 0x7fffffff : int(atomicAdd(&lw->zero_ctr[par], 1u));
+    named_bar_sync(bar, np);
+    const int z = *slot;
+    named_bar_sync(bar, np);
+    if (z >= s.zero_total) break;
+    zero_fill(p, s, z, pt, np);
+  }
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     fused_ep_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_w4,
                     const __grid_constant__ RowMaps rows_local,
@@ -1089,11 +1105,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (run_main && pusher && !(push_cta && p.push_bulk)) {
     // Loads and stores: push_warps warps of every computing CTA, or every
-    // warp of a push CTA.  Without push CTAs the same warps then zero the
-    // padded output rows (items after the push items).
+    // warp of a push CTA.  Without push CTAs the same warps then help the
+    // zero warps zero the padded output rows (the zero counter); computing
+    // CTAs that push beside push CTAs zero after their pushes (items after
+    // the push items).
     const int np = push_cta ? kThreads : p.push_warps * 32;  // threads taking part in each item
     const int pt = push_cta ? tid : tid - kWarpPush0 * 32;
-    const int last = push_cta ? s.push_total : s.push_total + s.zero_total;
+    const bool zero_counter = p.push_ctas == 0;
+    const int last = (push_cta || zero_counter) ? s.push_total : s.push_total + s.zero_total;
     const size_t row_bytes = size_t(p.H) * 2;
     bool pushes_done = false;
     for (;;) {
@@ -1149,6 +1168,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (pt == 0 && !pushes_done) atomicMax(&sm.push_end, static_cast<unsigned long long>(TRACE_NOW(p)));
+    if (zero_counter) zero_items(p, s, sm, lw, par, &sm.push_item, kNamedBarPush, np, pt);
+  } else if (run_main && p.push_ctas == 0 && p.push_warps + kZeroWarps <= kMaxPushWarps &&
+             warp >= kWarpPush0 + p.push_warps && warp < kWarpPush0 + p.push_warps + kZeroWarps) {
+    // Without push CTAs, kZeroWarps otherwise idle warps zero the padded
+    // output rows from the start, beside the push warps.
+    zero_items(p, s, sm, lw, par, &sm.zero_item, kNamedBarZero, kZeroWarps * 32,
+               tid - (kWarpPush0 + p.push_warps) * 32);
   } else if (run_main && push_cta && p.push_bulk && warp < kBulkStreams) {
     // Bulk copies: lane 0 of each stream warp moves its items through the
     // TMA engine — local rows into a ring of shared-memory pieces, each
@@ -1232,16 +1258,7 @@ __global__ void __launch_bounds__(kThreads, 1)
              warp < kWarpPush0 + kZeroWarps) {
     // With push CTAs, the computing CTAs' first push warps zero the padded
     // output rows (their own counter).
-    const int np = kZeroWarps * 32;
-    const int pt = tid - kWarpPush0 * 32;
-    for (;;) {
-      if (pt == 0) sm.zero_item = aborted(sm) ? 0x7fffffff : int(atomicAdd(&lw->zero_ctr[par], 1u));
-      named_bar_sync(kNamedBarPush, np);
-      const int z = sm.zero_item;
-      named_bar_sync(kNamedBarPush, np);
-      if (z >= s.zero_total) break;
-      zero_fill(p, s, z, pt, np);
-    }
+    zero_items(p, s, sm, lw, par, &sm.zero_item, kNamedBarPush, kZeroWarps * 32, tid - kWarpPush0 * 32);
   }
 
   // ---- teardown: drain in-flight copies and MMAs, free TMEM, publish "free".
