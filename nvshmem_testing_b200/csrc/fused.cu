@@ -92,6 +92,9 @@ constexpr int kRowMaps = 5;                     // B boxes of 8, 16, 32, 64, 128
 constexpr int kNamedBarPush = 1;
 constexpr int kNamedBarEpi = 2;                 // the epilogue warps (SwiGLU mode)
 constexpr int kNamedBarZero = 3;                // zero warps working beside the push warps
+// A pair whose first tile waits for remote rows prefetches the tile's first
+// weight k-blocks into L2 meanwhile: at most this many bytes over the grid.
+constexpr int64_t kPrefetchBudget = 64ll << 20;
 constexpr uint32_t kEpiStageBytes = kEpiWarps * 32 * 32 * 2;  // 32 rows x 32 features bf16 per warp
 
 struct Params {
@@ -844,6 +847,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           bool ok = t >= 0;
           if (ok) tl = decode_tile(s, W, El, me, p.local_first, t, p.merged);
+          if (ok && ti == 0 && p.w4 && tl.remote && !tile_rows_landed(p, s, tl)) {
+            // The pair's first tile waits for rows in flight (decode shapes:
+            // one tile per pair): stream the start of its weight slice into
+            // L2 meanwhile, both CTAs' feature halves, within the budget.
+            const int busy = max(1, min(s.npairs, s.tiles_total));
+            const int64_t fit = kPrefetchBudget / (int64_t(busy) * 2 * kABytes);
+            const int nk = fit < s.kblocks ? int(fit) : s.kblocks;
+            const int fa = tl.feat * kFeatPair;
+            const int rot0 = p.kstagger ? t % s.kblocks : 0;  // the k-block the tile starts at
+            for (int kb = 0; kb < nk; ++kb) {
+              const int kc = kb + rot0 < s.kblocks ? kb + rot0 : kb + rot0 - s.kblocks;
+              if (fa < p.N) tma_prefetch_l2_4d(&tm_w4, 0, kc * KB, fa / 64, tl.le);
+              if (fa + kFeatCta < p.N) tma_prefetch_l2_4d(&tm_w4, 0, kc * KB, (fa + kFeatCta) / 64, tl.le);
+            }
+          }
           const uint64_t tw0 = TRACE_NOW(p);
           if (ok && tl.remote) {
             const int* sg = s.seg + tl.le * (W + 1);

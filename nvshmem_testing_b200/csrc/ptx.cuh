@@ -120,6 +120,15 @@ __device__ __forceinline__ void tma_load_3d_pair(const CUtensorMap* map, uint32_
       : "memory");
 }
 
+// Bring one box of a tiled tensor map into L2 (no shared memory, no
+// completion to wait for).
+__device__ __forceinline__ void tma_prefetch_l2_4d(const CUtensorMap* map, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+
 __device__ __forceinline__ void tma_load_4d_pair(const CUtensorMap* map, uint32_t bar_cluster, void* dst, int c0,
                                                  int c1, int c2, int c3) {
   asm volatile(
