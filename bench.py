@@ -1141,6 +1141,7 @@ def main(argv=None) -> int:
                    "push_ctas": apg.placement(world, case.El)[0], "local_first": apg.placement(world, case.El)[1],
                    "push_warps": apg.push_setup()[0], "push_mode": apg.push_setup()[1],
                    "ready_first": apg.DEFAULT_READY_FIRST and world > 1, "merged": apg.DEFAULT_MERGED and world > 1,
+                   "row_groups": apg.DEFAULT_ROW_GROUPS,
                    "push_rows": apg.DEFAULT_PUSH_ROWS},
         "parity_vs_nccl_allclose": head["parity_vs_nccl_allclose"],
         "host_us_per_call": head["host_us_per_call"],
