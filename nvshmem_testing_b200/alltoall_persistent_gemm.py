@@ -89,6 +89,20 @@ def push_setup(push_warps: int | None = None, push_mode: int | None = None) -> t
     return pw, pm
 
 
+def sched_setup(W: int, ready_first: bool | None = None, merged: bool | None = None,
+                row_groups: int | None = None) -> int:
+    """The MOE_EP_SCHED_* word of a launch: ready-first and merged tiles
+    (only with more than one rank: one rank has no remote tiles) and the
+    remote row groups in bits 4-7 (0..15; 0 lets the kernel choose)."""
+    rf = DEFAULT_READY_FIRST if ready_first is None else bool(ready_first)
+    mg = DEFAULT_MERGED if merged is None else bool(merged)
+    rg = DEFAULT_ROW_GROUPS if row_groups is None else int(row_groups)
+    if not 0 <= rg <= 15:
+        raise ValueError(f"row_groups must be 0..15 (0: chosen by the kernel), got {rg}")
+    return ((N.SCHED_READY_FIRST if (rf and W > 1) else 0) | (N.SCHED_MERGED if (mg and W > 1) else 0) |
+            (rg << N.SCHED_ROW_GROUPS_SHIFT))
+
+
 def _group_info(group, world_size: int, rank: int) -> tuple[int, int]:
     if dist.is_available() and dist.is_initialized():
         return dist.get_rank(group), dist.get_world_size(group)
@@ -159,13 +173,7 @@ def _launch_params(me: int, W: int, tokens: torch.Tensor, gm: int | None, transm
     p.num_ctas = num_ctas
     p.push_ctas, p.local_first = placement(W, El, push_ctas, local_first)
     p.push_warps, p.push_mode = push_setup(push_warps, push_mode)
-    rf = DEFAULT_READY_FIRST if ready_first is None else bool(ready_first)
-    mg = DEFAULT_MERGED if merged is None else bool(merged)
-    rg = DEFAULT_ROW_GROUPS if row_groups is None else int(row_groups)
-    if not 0 <= rg <= 15:
-        raise ValueError(f"row_groups must be 0..15 (0: chosen by the kernel), got {rg}")
-    p.sched_mode = ((N.SCHED_READY_FIRST if (rf and W > 1) else 0) | (N.SCHED_MERGED if (mg and W > 1) else 0) |
-                    (rg << N.SCHED_ROW_GROUPS_SHIFT))
+    p.sched_mode = sched_setup(W, ready_first, merged, row_groups)
     p.counts_are_send = int(send_counts is not None)
     p.timeout_ns = int((timeout_s if timeout_s is not None else DEFAULT_TIMEOUT_S) * 1e9)
     p.status_host = ws.status_host.data_ptr()

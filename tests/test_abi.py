@@ -87,6 +87,23 @@ def test_bad_arguments_are_rejected_before_any_device_call():
     assert lib.moe_router(None, 0, 64, None, 16, 2, None, None, 1, None, None, None) == N.OK  # no tokens: nothing to do
 
 
+def test_launch_option_words():
+    """The host side of the placement and tile-order options: values the
+    kernel would reject never reach it."""
+    from nvshmem_testing_b200 import alltoall_persistent_gemm as apg
+    assert apg.placement(1, 4, 8, 4) == (0, 0)  # one rank: nothing to push, no remote tiles
+    assert apg.placement(8, 4, None, 99)[1] == 4  # local_first clamps to El
+    assert apg.push_setup(3, 8 | 2) == (3, 10)
+    for pw, pm in ((0, 0), (7, 0), (2, 16)):
+        with pytest.raises(ValueError):
+            apg.push_setup(pw, pm)
+    assert apg.sched_setup(1, True, True, 3) == 3 << 4  # one rank: no ready-first or merged tiles
+    assert apg.sched_setup(8, True, True, 7) == 1 | 2 | (7 << 4)
+    assert apg.sched_setup(2, False, False, 0) == 0
+    with pytest.raises(ValueError):
+        apg.sched_setup(2, False, False, 16)
+
+
 def test_status_word_decoding():
     assert N.decode_status_word((3 << 24) | (4 << 16) | 7) == (3, 4, 7)
 
