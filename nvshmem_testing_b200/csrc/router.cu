@@ -143,6 +143,65 @@ __device__ __forceinline__ int rt_xidx(int row, int col, int ep) {
   return row * ep + ((((col >> 2) ^ (row & 7))) << 2) + (col & 3);
 }
 
+// One owner row's softmax and top-k with its VPT values per thread held in
+// registers (TPR threads per row, thread `part` holding experts part,
+// part + TPR, ...): the same arithmetic, in the same order, as the shared-
+// memory form below.  Each probability becomes one 32-bit key, its bf16 bits
+// above (0xFFFF - expert): probabilities are >= 0, so the keys order like
+// the values, and equal values order by ascending expert id.  A top-k pick
+// is then one max over the thread's keys and one shuffle max over the row;
+// the picked key is unique and is cleared by the thread that holds it.
+template <int VPT, typename IdT>
+__device__ __forceinline__ void rt_row_topk_regs(const RouterArgs& a, const float* xbuf, int S, int R, int TPR,
+                                                 int lr, int part, int64_t t, bool live) {
+  const int E = a.E, K = a.K;
+  float lv[VPT];
+  float m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int e = part + j * TPR;
+    lv[j] = -INFINITY;
+    if (e < E) {
+      const int xi = rt_xidx(lr, e, a.ep);
+      float sum = 0.f;
+      for (int q = 0; q < S; ++q) sum += xbuf[q * R * a.ep + xi];
+      const __nv_bfloat16 lb = __float2bfloat16_rn(sum);
+      if (live) a.logits[t * E + e] = lb;
+      lv[j] = __bfloat162float(lb);
+      m = fmaxf(m, lv[j]);
+    }
+  }
+  for (int o = 1; o < TPR; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float z = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j)
+    if (part + j * TPR < E) z += expf(lv[j] - m);
+  for (int o = 1; o < TPR; o <<= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
+  uint32_t key[VPT];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int e = part + j * TPR;
+    key[j] = 0u;
+    if (e < E) {
+      const __nv_bfloat16 pb = __float2bfloat16_rn(expf(lv[j] - m) / z);
+      key[j] = (uint32_t(__bfloat16_as_ushort(pb)) << 16) | uint32_t(0xFFFF - e);
+    }
+  }
+  IdT* ids = static_cast<IdT*>(a.ids);
+  for (int k = 0; k < K; ++k) {
+    uint32_t b = 0u;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) b = max(b, key[j]);
+    for (int o = 1; o < TPR; o <<= 1) b = max(b, __shfl_xor_sync(0xffffffffu, b, o));
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) key[j] = key[j] == b ? 0u : key[j];
+    if (part == 0 && live) {
+      ids[t * K + k] = static_cast<IdT>(0xFFFF - int(b & 0xFFFFu));
+      a.vals[t * K + k] = __uint_as_float(b & 0xFFFF0000u);
+    }
+  }
+}
+
 template <typename IdT>
 __global__ void __launch_bounds__(kRtThreads, 1)
     router_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_r,
@@ -285,6 +344,12 @@ __global__ void __launch_bounds__(kRtThreads, 1)
   const int lr = int(threadIdx.x) / TPR, part = int(threadIdx.x) % TPR;
   const int64_t t = m0 + int64_t(r) * R + lr;
   const bool live = t < a.T;  // rows past T compute (zeros) but write nothing
+  const int vpt = (E + TPR - 1) / TPR;
+  if (vpt <= 8) rt_row_topk_regs<8, IdT>(a, xbuf, S, R, TPR, lr, part, t, live);
+  else if (vpt <= 16) rt_row_topk_regs<16, IdT>(a, xbuf, S, R, TPR, lr, part, t, live);
+  else {
+  // More than 16 values per thread (one or two CTAs per tile and E > 64):
+  // the values stay in the exchange buffer.
   float m = -INFINITY;
   for (int e = part; e < E; e += TPR) {
     const int xi = rt_xidx(lr, e, a.ep);
@@ -329,6 +394,7 @@ __global__ void __launch_bounds__(kRtThreads, 1)
       ids[t * K + k] = static_cast<IdT>(be);
       a.vals[t * K + k] = best;
     }
+  }
   }
 
   // Teardown: after an abort, wait (bounded) for every issued load and MMA.
