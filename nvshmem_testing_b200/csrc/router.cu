@@ -146,26 +146,35 @@ __device__ __forceinline__ int rt_xidx(int row, int col, int ep) {
 // One owner row's softmax and top-k with its VPT values per thread held in
 // registers (TPR threads per row, thread `part` holding experts part,
 // part + TPR, ...): the same arithmetic, in the same order, as the shared-
-// memory form below.  Each probability becomes one 32-bit key, its bf16 bits
-// above (0xFFFF - expert): probabilities are >= 0, so the keys order like
-// the values, and equal values order by ascending expert id.  A top-k pick
-// is then one max over the thread's keys and one shuffle max over the row;
-// the picked key is unique and is cleared by the thread that holds it.
+// memory form below.  The S partial sums are read one source block at a
+// time, all VPT loads of a block in flight together, before any store (a
+// store between them would order every later load behind it).  Each
+// probability then becomes one 32-bit key, its bf16 bits above
+// (0xFFFF - expert), kept in the same registers: probabilities are >= 0, so
+// the keys order like the values, and equal values order by ascending
+// expert id.  A top-k pick is one max over the thread's keys and one shuffle
+// max over the row; the picked key is unique and is cleared where it is held.
 template <int VPT, typename IdT>
 __device__ __forceinline__ void rt_row_topk_regs(const RouterArgs& a, const float* xbuf, int S, int R, int TPR,
                                                  int lr, int part, int64_t t, bool live) {
   const int E = a.E, K = a.K;
   float lv[VPT];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) lv[j] = 0.f;
+  for (int q = 0; q < S; ++q) {
+    const float* blk = xbuf + q * R * a.ep;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int e = part + j * TPR;
+      if (e < E) lv[j] += blk[rt_xidx(lr, e, a.ep)];
+    }
+  }
   float m = -INFINITY;
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int e = part + j * TPR;
-    lv[j] = -INFINITY;
     if (e < E) {
-      const int xi = rt_xidx(lr, e, a.ep);
-      float sum = 0.f;
-      for (int q = 0; q < S; ++q) sum += xbuf[q * R * a.ep + xi];
-      const __nv_bfloat16 lb = __float2bfloat16_rn(sum);
+      const __nv_bfloat16 lb = __float2bfloat16_rn(lv[j]);
       if (live) a.logits[t * E + e] = lb;
       lv[j] = __bfloat162float(lb);
       m = fmaxf(m, lv[j]);
@@ -177,24 +186,24 @@ __device__ __forceinline__ void rt_row_topk_regs(const RouterArgs& a, const floa
   for (int j = 0; j < VPT; ++j)
     if (part + j * TPR < E) z += expf(lv[j] - m);
   for (int o = 1; o < TPR; o <<= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
-  uint32_t key[VPT];
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int e = part + j * TPR;
-    key[j] = 0u;
+    uint32_t key = 0u;
     if (e < E) {
       const __nv_bfloat16 pb = __float2bfloat16_rn(expf(lv[j] - m) / z);
-      key[j] = (uint32_t(__bfloat16_as_ushort(pb)) << 16) | uint32_t(0xFFFF - e);
+      key = (uint32_t(__bfloat16_as_ushort(pb)) << 16) | uint32_t(0xFFFF - e);
     }
+    lv[j] = __uint_as_float(key);  // the key's bits, never used as a number
   }
   IdT* ids = static_cast<IdT*>(a.ids);
   for (int k = 0; k < K; ++k) {
     uint32_t b = 0u;
 #pragma unroll
-    for (int j = 0; j < VPT; ++j) b = max(b, key[j]);
+    for (int j = 0; j < VPT; ++j) b = max(b, __float_as_uint(lv[j]));
     for (int o = 1; o < TPR; o <<= 1) b = max(b, __shfl_xor_sync(0xffffffffu, b, o));
 #pragma unroll
-    for (int j = 0; j < VPT; ++j) key[j] = key[j] == b ? 0u : key[j];
+    for (int j = 0; j < VPT; ++j) lv[j] = __float_as_uint(lv[j]) == b ? 0.f : lv[j];
     if (part == 0 && live) {
       ids[t * K + k] = static_cast<IdT>(0xFFFF - int(b & 0xFFFFu));
       a.vals[t * K + k] = __uint_as_float(b & 0xFFFF0000u);
@@ -347,9 +356,10 @@ __global__ void __launch_bounds__(kRtThreads, 1)
   const int vpt = (E + TPR - 1) / TPR;
   if (vpt <= 8) rt_row_topk_regs<8, IdT>(a, xbuf, S, R, TPR, lr, part, t, live);
   else if (vpt <= 16) rt_row_topk_regs<16, IdT>(a, xbuf, S, R, TPR, lr, part, t, live);
+  else if (vpt <= 32) rt_row_topk_regs<32, IdT>(a, xbuf, S, R, TPR, lr, part, t, live);
   else {
-  // More than 16 values per thread (one or two CTAs per tile and E > 64):
-  // the values stay in the exchange buffer.
+  // More than 32 values per thread (one CTA per tile and E > 128): the
+  // values stay in the exchange buffer.
   float m = -INFINITY;
   for (int e = part; e < E; e += TPR) {
     const int xi = rt_xidx(lr, e, a.ep);
