@@ -316,9 +316,13 @@ __global__ void __launch_bounds__(kRtThreads, 1)
   const int owner = row / R, lrow = row % R;
   const uint32_t blk = smem_u32(xbuf) + uint32_t(r * R * a.ep) * 4u;
   const uint32_t dst_blk = S > 1 ? mapa_shared(blk, uint32_t(owner)) : blk;
-  // 64 columns per round: two TMEM loads behind one wait.
+  // 64 columns per round: two TMEM loads behind one wait.  Rows past T (the
+  // last tile, small decode batches) are not sent; a warp none of whose 32
+  // rows is a token skips its TMEM loads too.
   const uint32_t trow = tmem + (uint32_t(quarter * 32) << 16);
-  for (int c0 = (warp >> 2) * 64; c0 < a.ep; c0 += (kRtThreads / 128) * 64) {
+  const bool row_live = m0 + row < a.T;
+  const bool warp_live = __any_sync(0xffffffffu, row_live);
+  for (int c0 = (warp >> 2) * 64; warp_live && c0 < a.ep; c0 += (kRtThreads / 128) * 64) {
     uint32_t v0[32], v1[32];
     const bool l0 = ok && c0 < a.n_mma, l1 = ok && c0 + 32 < a.n_mma;
     if (l0) tmem_ld_32x32b_x32(trow + uint32_t(c0), v0);
@@ -330,7 +334,7 @@ __global__ void __launch_bounds__(kRtThreads, 1)
       if (!l1) v1[j] = 0u;
     }
 #pragma unroll
-    for (int j = 0; j < 32; j += 4) {
+    for (int j = 0; j < 32 && row_live; j += 4) {
       st_shared_cluster_v4(dst_blk + uint32_t(rt_xidx(lrow, c0 + j, a.ep)) * 4u, v0[j], v0[j + 1], v0[j + 2],
                            v0[j + 3]);
       if (c0 + 32 < a.ep)
@@ -352,9 +356,12 @@ __global__ void __launch_bounds__(kRtThreads, 1)
   const int TPR = kRtThreads / R;  // 4 * S: 4..32, a power of two dividing 32
   const int lr = int(threadIdx.x) / TPR, part = int(threadIdx.x) % TPR;
   const int64_t t = m0 + int64_t(r) * R + lr;
-  const bool live = t < a.T;  // rows past T compute (zeros) but write nothing
+  // Rows past T were not exchanged: a warp with no live row skips them; in
+  // a warp with some, they compute on stale values and write nothing.
+  const bool live = t < a.T;
   const int vpt = (E + TPR - 1) / TPR;
-  if (vpt <= 8) rt_row_topk_regs<8, IdT>(a, xbuf, S, R, TPR, lr, part, t, live);
+  if (!__any_sync(0xffffffffu, live)) {
+  } else if (vpt <= 8) rt_row_topk_regs<8, IdT>(a, xbuf, S, R, TPR, lr, part, t, live);
   else if (vpt <= 16) rt_row_topk_regs<16, IdT>(a, xbuf, S, R, TPR, lr, part, t, live);
   else if (vpt <= 32) rt_row_topk_regs<32, IdT>(a, xbuf, S, R, TPR, lr, part, t, live);
   else {
